@@ -1,0 +1,429 @@
+"""Benchmark of the attention-backward path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload flux|cross|fp16|video] [--no-cpu-baseline]
+
+One step = one backward pass (dQ, dK, dV) over the workload's heads on each
+GPU. The default workload is FLUX-like joint self-attention (M=N=4608, d=128,
+24 heads, bf16). With N GPUs (launched under torchrun, one rank per GPU),
+each rank runs its own 24-head shard of a 24*N-head batch (weak scaling: the
+heads are independent, so there is no collective on the data path); NCCL
+only gathers per-rank timings and output checksums after the timed region.
+
+Reported (one JSON line from rank 0):
+  value       counted TFLOP/s (8*M*N*d*heads, all ranks) / max-over-ranks
+              device time of K back-to-back steps, inputs resident in HBM
+              (P alone is 1.02 GB per GPU, far larger than the 126 MB L2, so
+              no L2 flush is needed between steps)
+  e2e         the same metric through the reference-facing C-ABI call
+              (fmha_bwd_full_py) with host buffers: pinned-host -> device
+              copies of Q, K, V, P, dO and device -> host copies of dQ, dK, dV
+              inside the timed region, every step
+  roofline    the main (fused) kernel: counted FLOPs per launch / its mean
+              CUDA-event duration, against the measured bf16 peak
+  cpu_baseline  the reference's own CPU backward (cpu_reference.hpp), timed
+              on this host's cores on a bounded sample (rank 0, N=1 only)
+
+--impl reference times the reference's CPU implementation of the path (the
+reference's GPU code is HIP for gfx1100 and cannot run here) on the same
+workload, metric and unit: each step is a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "fmha-bwd-gfx1100_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "bwd TFLOP/s (8·M·N·d·H/t) at M=N=4608,d=128,H=24; % of B200 bf16 peak"
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    try:
+        with open(PEAKS_FILE) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic(key: str):
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary
+    (lines 'key: bytes'), or None."""
+    try:
+        with open(TRAFFIC_FILE) as f:
+            for line in f:
+                if ":" in line and not line.lstrip().startswith("#"):
+                    k, v = line.split(":", 1)
+                    if k.strip() == key:
+                        return float(v.split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    QUERY = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.path = os.path.join("/tmp", f"fmha_bench_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            args = ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                    "-lms", "100"]
+            if self.uuid:
+                args += ["-i", self.uuid]
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(args, stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 10:
+                    continue
+                try:
+                    rows.append({"sm": float(parts[2]), "max": float(parts[3]),
+                                 "power": float(parts[4]), "hw": parts[6], "hwt": parts[7],
+                                 "swt": parts[8], "pcap": parts[9]})
+                except ValueError:
+                    continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        reasons = set()
+        for r in rows:
+            if r["hw"] == "Active":
+                reasons.add("hw_slowdown")
+            if r["hwt"] == "Active":
+                reasons.add("hw_thermal_slowdown")
+            if r["swt"] == "Active":
+                reasons.add("sw_thermal_slowdown")
+            if r["pcap"] == "Active":
+                reasons.add("sw_power_cap")
+        loaded = [r["sm"] for r in rows if r["power"] > 200.0] or [r["sm"] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(r["max"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows),
+                "power_w_max": max(r["power"] for r in rows)}
+
+
+# ------------------------------------------------------- CPU (reference) leg
+def cpu_reference_sample(w, rows: int, threads: int, seed: int = 42):
+    """Time the reference's own fmha_backward_cpu on `threads` heads of the
+    workload, each restricted to its first `rows` query rows (all N keys, full
+    d), one head per thread. Returns (flops, seconds, kind, cores)."""
+    from oracle import oracle as O
+
+    kind = "reference" if O.have_reference() else "port"
+    Q, K, V, P, dO = O.make_inputs(rows, w.N, w.d, threads, w.dtype, seed=seed,
+                                   do_std=w.do_std)
+    t0 = time.perf_counter()
+    if kind == "reference":
+        O.reference_bwd(Q, K, V, P, dO, w.dtype, threads=threads)
+    else:
+        O.oracle_bwd(Q, K, V, P, dO, w.dtype, threads=threads)
+    dt = time.perf_counter() - t0
+    return 8.0 * rows * w.N * w.d * threads, dt, kind, threads
+
+
+def cpu_threads(w) -> int:
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    return max(1, min(n, w.heads))
+
+
+# ------------------------------------------------------------------ helpers
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def run_reference_arm(args, w):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    threads = cpu_threads(w)
+    rows = args.cpu_rows_per_step
+    for _ in range(args.warmup):
+        cpu_reference_sample(w, rows, threads)
+    times, flops, kind = [], 0.0, "reference"
+    for _ in range(args.steps):
+        fl, dt, kind, _ = cpu_reference_sample(w, rows, threads)
+        times.append(dt)
+        flops = fl
+    total = sum(times)
+    value = flops * len(times) / total / 1e12
+    line = {
+        "impl": "reference",
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": w.dtype, "data": "synthetic",
+        "config": {"workload": w.description, "M": w.M, "N": w.N, "d": w.d,
+                   "heads_per_gpu": w.heads, "parallelism": "cpu threads over heads"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+                         "sample": f"per step: first {rows} of {w.M} query rows x {w.N} keys x "
+                                   f"d={w.d} for {threads} heads, one head per thread "
+                                   "(reference fmha_backward_cpu, cpu_reference.hpp:74-126)"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference's GPU path is HIP/rocWMMA for gfx1100 and cannot run on B200; "
+                "its CPU implementation of the same path is the reference arm",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="flux")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-rows", type=int, default=512,
+                    help="query rows per head in the CPU baseline sample")
+    ap.add_argument("--cpu-rows-per-step", type=int, default=128,
+                    help="query rows per head per step of the reference arm")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    import workloads
+
+    w = workloads.WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return run_reference_arm(args, w)
+
+    import torch
+    import torch.distributed as dist
+
+    import fmha_bwd_b200 as F
+
+    rank, world, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+
+    # ---- inputs: this rank's head shard of a (heads * world)-head batch
+    heads = w.heads
+    Q, K, V, P, dO = workloads.make_inputs(w, seed=42, device=dev, heads=heads,
+                                           head_offset=rank * heads)
+    dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
+    lib = F.load_library(w.torch_dtype)
+    import ctypes
+
+    ev_fn = lib.fmha_bwd_full_stream_events if w.dtype == "bf16" else \
+        lib.fmha_bwd_full_fp16_stream_events
+    ev_fn.argtypes = [ctypes.c_void_p] * 8 + [ctypes.c_int] * 4 + [ctypes.c_void_p,
+                                                                   ctypes.c_void_p]
+    ev_fn.restype = ctypes.c_int
+    stream = torch.cuda.Stream(device=dev)
+    ptrs = (dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), Q.data_ptr(), K.data_ptr(),
+            V.data_ptr(), P.data_ptr(), dO.data_ptr(), w.M, w.N, w.d, heads)
+
+    def step(events_arr=None):
+        rc = ev_fn(*ptrs, ctypes.c_void_p(stream.cuda_stream),
+                   ctypes.cast(events_arr, ctypes.c_void_p) if events_arr is not None else None)
+        if rc != 0:
+            raise F.FmhaBwdError(rc, lib.fmha_bwd_last_error_message().decode())
+
+    torch.cuda.synchronize(dev)
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    if lib.fmha_bwd_poll_device_status() != 0:
+        raise RuntimeError("device status reported a wait timeout during warm-up")
+
+    # per-step kernel-boundary events, to time the main kernel inside the run
+    K_steps = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K_steps)]
+    ev_arrays = []
+    for e4 in evs:
+        arr = (ctypes.c_void_p * 4)(*[e.cuda_event for e in e4])
+        ev_arrays.append(arr)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    start.record(stream)
+    for k in range(K_steps):
+        step(ev_arrays[k])
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms_total = start.elapsed_time(end)
+    if lib.fmha_bwd_poll_device_status() != 0:
+        raise RuntimeError("device status reported a wait timeout in the timed region")
+    t_rowsum = [e[0].elapsed_time(e[1]) for e in evs]
+    t_main = [e[1].elapsed_time(e[2]) for e in evs]
+    t_fin = [e[2].elapsed_time(e[3]) for e in evs]
+
+    # ---- gather timings and checksums (NCCL, after the timed region)
+    checksum = float(dQ.float().sum().item() + dK.float().sum().item() + dV.float().sum().item())
+    if world > 1:
+        t = torch.tensor([ms_total, statistics.mean(t_main), checksum], device=dev,
+                         dtype=torch.float64)
+        allt = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allt, t)
+        allt = torch.stack(allt).cpu()
+        ms_max = float(allt[:, 0].max())
+        main_ms = float(allt[:, 1].max())
+        checksums = [float(x) for x in allt[:, 2]]
+    else:
+        ms_max = ms_total
+        main_ms = statistics.mean(t_main)
+        checksums = [checksum]
+
+    flops_rank = w.flops(heads)
+    total_flops = flops_rank * world * K_steps
+    value = total_flops / (ms_max * 1e-3) / 1e12
+    ms_per_step = ms_max / K_steps
+
+    # ---- e2e through the reference-facing call with host buffers
+    e2e = None
+    if args.e2e_steps > 0:
+        hQ, hK, hV, hP, hdO = (t.cpu().pin_memory() for t in (Q, K, V, P, dO))
+        ohQ, ohK, ohV = (torch.empty_like(t, device="cpu").pin_memory() for t in (Q, K, V))
+        dQ2, dK2, dV2 = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
+        dev_in = [torch.empty_like(t) for t in (Q, K, V, P, dO)]
+        h2d = sum(t.numel() * t.element_size() for t in (hQ, hK, hV, hP, hdO))
+        d2h = sum(t.numel() * t.element_size() for t in (ohQ, ohK, ohV))
+        full = lib.fmha_bwd_full_py if w.dtype == "bf16" else lib.fmha_bwd_full_fp16
+
+        def e2e_step():
+            for dst, src in zip(dev_in, (hQ, hK, hV, hP, hdO)):
+                dst.copy_(src, non_blocking=True)
+            full(dQ2.data_ptr(), dK2.data_ptr(), dV2.data_ptr(),
+                 *(t.data_ptr() for t in dev_in), w.M, w.N, w.d, heads)
+            for dst, src in zip((ohQ, ohK, ohV), (dQ2, dK2, dV2)):
+                dst.copy_(src, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        s1.record()
+        torch.cuda.synchronize(dev)
+        e2e_ms = s0.elapsed_time(s1)
+        if lib.fmha_bwd_last_error() != 0:
+            raise RuntimeError(lib.fmha_bwd_last_error_message().decode())
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": flops_rank * world * args.e2e_steps / (e2e_ms * 1e-3) / 1e12,
+               "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": e2e_ms / args.e2e_steps,
+               "entry": "fmha_bwd_full_py" if w.dtype == "bf16" else "fmha_bwd_full_fp16"}
+        if not torch.equal(dK2, dK) or not torch.equal(dV2, dV):
+            raise RuntimeError("e2e outputs differ from the device-resident run")
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    peaks, peak_src = load_peaks()
+    peak = float(peaks["bf16_tflops"])
+    peak_sus = float(peaks.get("bf16_tflops_sustained", peak))
+    achieved = flops_rank / (main_ms * 1e-3) / 1e12
+    rowsum_ms = statistics.mean(t_rowsum)
+    fin_ms = statistics.mean(t_fin)
+    traffic = load_traffic(f"main_kernel:{w.name}")
+    roofline = {
+        "kernel": "main_kernel (fused dP, dS, dV, dK, dQ-partials)",
+        "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+        "frac": achieved / peak, "traffic": traffic,
+        "peak_source": f"{peak_src} (bf16 burst, MEASURED_PEAKS.json)" if peak_src == "measured"
+        else "fallback 1.59 PFLOP/s",
+        "frac_of_sustained": achieved / peak_sus,
+        "kernel_ms": {"rowsum": rowsum_ms, "main": main_ms, "dq_finalize": fin_ms},
+        "step_frac_of_peak": value / world / peak,
+    }
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": K_steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": w.dtype, "data": "synthetic",
+        "config": {"workload": w.description, "M": w.M, "N": w.N, "d": w.d,
+                   "heads_per_gpu": heads, "total_heads": heads * world,
+                   "parallelism": f"head-sharded x{world}, no data-path collective",
+                   "l2": "inputs larger than L2 (P is 1.02 GB per GPU vs 126 MB L2); no flush"},
+        "e2e": e2e,
+        "gpu_launches": 3 * K_steps,
+        "roofline": roofline,
+        "clocks": clocks,
+        "checksums": checksums,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        threads = cpu_threads(w)
+        fl, dt, kind, cores = cpu_reference_sample(w, args.cpu_rows, threads)
+        line["cpu_baseline"] = {
+            "value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": kind,
+            "sample": f"first {args.cpu_rows} of {w.M} query rows x {w.N} keys x d={w.d} for "
+                      f"{threads} heads, one head per thread, {dt:.1f} s",
+        }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,36 @@
+// extern "C" entry points shared by both libraries (error reporting and the
+// wait-timeout setting). Included by exactly one translation unit per
+// library, after fmha_bwd_launch.cuh.
+#pragma once
+
+#include "fmha_bwd_launch.cuh"
+
+// Exported entry points stay visible when the library is built with
+// -fvisibility=hidden (everything else is internal).
+#define FMHA_API __attribute__((visibility("default")))
+
+extern "C" {
+
+FMHA_API int fmha_bwd_last_error(void) { return fmha_sm100::error_state().code.load(); }
+
+FMHA_API const char* fmha_bwd_last_error_message(void) { return fmha_sm100::error_state().message; }
+
+FMHA_API int fmha_bwd_poll_device_status(void) {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) {
+    cudaGetLastError();
+    return fmha_sm100::kErrLaunch;
+  }
+  std::lock_guard<std::mutex> g(fmha_sm100::ws_mutex());
+  auto& m = fmha_sm100::ws_map();
+  auto it = m.find(device);
+  if (it == m.end() || it->second.host_status == nullptr) return fmha_sm100::kOk;
+  const fmha_sm100::KernelStatus st = fmha_sm100::read_status(it->second.host_status);
+  return st.code != 0 ? fmha_sm100::kErrDeviceTimeout : fmha_sm100::kOk;
+}
+
+FMHA_API void fmha_bwd_set_wait_timeout_ms(int ms) {
+  fmha_sm100::timeout_override_ns().store(ms > 0 ? static_cast<uint64_t>(ms) * 1000000ull : 0ull);
+}
+
+}  // extern "C"

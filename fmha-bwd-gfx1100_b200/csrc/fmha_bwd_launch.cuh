@@ -1,0 +1,327 @@
+// Host side of the attention-backward C-ABI: argument checks, per-device
+// workspace, TMA tensor maps and the three launches. Included once by each
+// library translation unit (bf16 and fp16), which instantiates it for its
+// element type and defines the extern "C" entry points.
+//
+// Replaces the body of fmha_bwd_full_py (src/fmha_bwd_kernels.hip:475-523)
+// and fmha_bwd_full_fp16 (src/fmha_bwd_kernels_fp16.hip:236-280):
+//   * no per-call dP/dS allocation (those never leave the SM); the workspace
+//     is H*M fp32 rowsums + H*M*d fp32 dQ accumulator, cached per device and
+//     grown on demand;
+//   * shapes and pointers are checked before anything is launched, so a bad
+//     call leaves the outputs untouched and reports an error code;
+//   * 64-bit offsets throughout.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+
+#include "fmha_bwd_kernels.cuh"
+
+namespace fmha_sm100 {
+
+// Error codes returned by the entry points and by fmha_bwd_last_error().
+enum FmhaError : int {
+  kOk = 0,
+  kErrInvalidArgument = 1,   // null pointer, non-positive or unsupported size
+  kErrMisaligned = 2,        // pointer or row pitch not 16-byte aligned
+  kErrUnsupportedDevice = 3, // not an sm_100 device
+  kErrOutOfMemory = 4,       // workspace allocation failed
+  kErrLaunch = 5,            // CUDA launch or runtime error
+  kErrDeviceTimeout = 6,     // an in-kernel wait ran out of time (see status)
+  kErrNoDriver = 7,          // cuTensorMapEncodeTiled unavailable
+};
+
+struct ErrorState {
+  std::atomic<int> code{0};
+  std::mutex mu;
+  char message[512] = {0};
+};
+
+inline ErrorState& error_state() {
+  static ErrorState s;
+  return s;
+}
+
+inline int set_error(int code, const char* fmt, ...) {
+  ErrorState& s = error_state();
+  std::lock_guard<std::mutex> g(s.mu);
+  s.code.store(code);
+  if (code == kOk) {
+    s.message[0] = 0;
+    return code;
+  }
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(s.message, sizeof(s.message), fmt, ap);
+  va_end(ap);
+  fprintf(stderr, "fmha_bwd: %s\n", s.message);
+  return code;
+}
+
+// ---------------------------------------------------------------- driver
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 3-D map over a [heads][rows][cols] row-major 16-bit tensor, box of
+// 64 columns x 128 rows x 1 head, 128-byte swizzle, zero fill out of bounds.
+inline bool encode_map(CUtensorMap* map, bool bf16, const void* base, uint64_t cols,
+                       uint64_t rows, uint64_t heads) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {cols, rows, heads};
+  const cuuint64_t strides[2] = {cols * 2, rows * cols * 2};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kBoxCols), static_cast<cuuint32_t>(kTile), 1};
+  const cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ------------------------------------------------------------- workspace
+struct DeviceWorkspace {
+  float* dsum = nullptr;
+  size_t dsum_floats = 0;
+  float* dqacc = nullptr;
+  size_t dqacc_floats = 0;
+  KernelStatus* status = nullptr;       // device memory
+  KernelStatus* host_status = nullptr;  // mapped pinned host memory
+  KernelStatus* host_status_dev = nullptr;
+  bool attrs_set = false;
+  int sm_count = 0;
+};
+
+inline std::mutex& ws_mutex() {
+  static std::mutex m;
+  return m;
+}
+inline std::map<int, DeviceWorkspace>& ws_map() {
+  static std::map<int, DeviceWorkspace> m;
+  return m;
+}
+
+inline uint64_t wait_timeout_ns() {
+  static std::atomic<uint64_t> cached{0};
+  uint64_t v = cached.load();
+  if (v == 0) {
+    uint64_t ms = 4000;
+    if (const char* e = getenv("FMHA_BWD_WAIT_TIMEOUT_MS")) {
+      long long x = atoll(e);
+      if (x > 0) ms = static_cast<uint64_t>(x);
+    }
+    v = ms * 1000000ull;
+    cached.store(v);
+  }
+  return v;
+}
+
+inline std::atomic<uint64_t>& timeout_override_ns() {
+  static std::atomic<uint64_t> v{0};
+  return v;
+}
+
+inline uint64_t effective_timeout_ns() {
+  uint64_t o = timeout_override_ns().load();
+  return o ? o : wait_timeout_ns();
+}
+
+template <typename T>
+void set_kernel_attrs() {
+  cudaFuncSetAttribute(rowsum_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       RowsumCfg<64>::kSmemBytes);
+  cudaFuncSetAttribute(rowsum_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       RowsumCfg<128>::kSmemBytes);
+  cudaFuncSetAttribute(main_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       MainCfg<64>::kSmemBytes);
+  cudaFuncSetAttribute(main_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       MainCfg<128>::kSmemBytes);
+}
+
+// Returns the workspace of the current device with at least the requested
+// capacity, or nullptr (error already recorded).
+template <typename T>
+DeviceWorkspace* get_workspace(int device, size_t dsum_floats, size_t dqacc_floats) {
+  std::lock_guard<std::mutex> g(ws_mutex());
+  DeviceWorkspace& w = ws_map()[device];
+  if (!w.status) {
+    if (cudaMalloc(&w.status, sizeof(KernelStatus)) != cudaSuccess) {
+      set_error(kErrOutOfMemory, "status word allocation failed");
+      return nullptr;
+    }
+    cudaMemset(w.status, 0, sizeof(KernelStatus));
+    if (cudaHostAlloc(&w.host_status, sizeof(KernelStatus),
+                      cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess ||
+        cudaHostGetDevicePointer(&w.host_status_dev, w.host_status, 0) != cudaSuccess) {
+      set_error(kErrOutOfMemory, "host status slot allocation failed");
+      return nullptr;
+    }
+    memset(w.host_status, 0, sizeof(KernelStatus));
+    cudaDeviceGetAttribute(&w.sm_count, cudaDevAttrMultiProcessorCount, device);
+  }
+  if (!w.attrs_set) {
+    set_kernel_attrs<T>();
+    w.attrs_set = true;
+  }
+  if (dsum_floats > w.dsum_floats) {
+    if (w.dsum) cudaFree(w.dsum);
+    w.dsum = nullptr;
+    w.dsum_floats = 0;
+    if (cudaMalloc(&w.dsum, dsum_floats * sizeof(float)) != cudaSuccess) {
+      cudaGetLastError();
+      set_error(kErrOutOfMemory, "workspace allocation of %zu bytes failed",
+                dsum_floats * sizeof(float));
+      return nullptr;
+    }
+    w.dsum_floats = dsum_floats;
+  }
+  if (dqacc_floats > w.dqacc_floats) {
+    if (w.dqacc) cudaFree(w.dqacc);
+    w.dqacc = nullptr;
+    w.dqacc_floats = 0;
+    if (cudaMalloc(&w.dqacc, dqacc_floats * sizeof(float)) != cudaSuccess) {
+      cudaGetLastError();
+      set_error(kErrOutOfMemory, "workspace allocation of %zu bytes failed",
+                dqacc_floats * sizeof(float));
+      return nullptr;
+    }
+    w.dqacc_floats = dqacc_floats;
+  }
+  return &w;
+}
+
+// Field-wise volatile read of a status slot written by the device.
+inline KernelStatus read_status(const KernelStatus* p) {
+  const volatile int* v = reinterpret_cast<const volatile int*>(p);
+  KernelStatus s;
+  s.code = v[0];
+  s.where = v[1];
+  s.block = v[2];
+  s.pad = 0;
+  return s;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Validates the call. Returns kOk or an error code (already recorded).
+inline int check_args(const void* dQ, const void* dK, const void* dV, const void* Q,
+                      const void* K, const void* V, const void* P, const void* dO, int M,
+                      int N, int D, int H) {
+  if (!dQ || !dK || !dV || !Q || !K || !V || !P || !dO)
+    return set_error(kErrInvalidArgument, "null pointer argument");
+  if (M <= 0 || N <= 0 || H <= 0 || D <= 0)
+    return set_error(kErrInvalidArgument, "sizes must be positive (M=%d N=%d K_dim=%d heads=%d)", M,
+                     N, D, H);
+  if (D != 64 && D != 128)
+    return set_error(kErrInvalidArgument, "K_dim=%d unsupported (64 or 128)", D);
+  if (H > 65535) return set_error(kErrInvalidArgument, "total_heads=%d exceeds 65535", H);
+  if (N % 8 != 0)
+    return set_error(kErrMisaligned, "N=%d: P rows must be a multiple of 16 bytes (N %% 8 == 0)", N);
+  if (!aligned16(dQ) || !aligned16(dK) || !aligned16(dV) || !aligned16(Q) || !aligned16(K) ||
+      !aligned16(V) || !aligned16(P) || !aligned16(dO))
+    return set_error(kErrMisaligned, "every buffer must be 16-byte aligned");
+  return kOk;
+}
+
+// Launches the three kernels on `stream`. When `sync` is set, waits for the
+// stream and reports in-kernel wait timeouts as kErrDeviceTimeout.
+template <typename T>
+int run_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const T* P,
+                 const T* dO, int M, int N, int D, int H, cudaStream_t stream, bool sync,
+                 cudaEvent_t const* events = nullptr) {
+  int rc = check_args(dQ, dK, dV, Q, K, V, P, dO, M, N, D, H);
+  if (rc != kOk) return rc;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(kErrLaunch, "no current CUDA device");
+  }
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (major != 10 || minor != 0)
+    return set_error(kErrUnsupportedDevice, "device %d is sm_%d%d; this library needs sm_100", device,
+                     major, minor);
+  const size_t rows = static_cast<size_t>(H) * static_cast<size_t>(M);
+  DeviceWorkspace* w = get_workspace<T>(device, rows, rows * static_cast<size_t>(D));
+  if (!w) return kErrOutOfMemory;
+
+  constexpr bool kBF16 = Elem<T>::kBF16;
+  CUtensorMap mQ, mK, mV, mdO, mP;
+  if (!encode_fn()) return set_error(kErrNoDriver, "cuTensorMapEncodeTiled is unavailable");
+  if (!encode_map(&mQ, kBF16, Q, D, M, H) || !encode_map(&mK, kBF16, K, D, N, H) ||
+      !encode_map(&mV, kBF16, V, D, N, H) || !encode_map(&mdO, kBF16, dO, D, M, H) ||
+      !encode_map(&mP, kBF16, P, N, M, H))
+    return set_error(kErrInvalidArgument, "tensor map encoding failed (M=%d N=%d K_dim=%d heads=%d)",
+                     M, N, D, H);
+
+  const uint64_t tmo = effective_timeout_ns();
+  // Optional timing events at the kernel boundaries: [0] before the rowsum
+  // kernel, [1] before the main kernel, [2] before dQ finalize, [3] after it.
+  auto mark = [&](int k) {
+    if (events && events[k]) cudaEventRecord(events[k], stream);
+  };
+  mark(0);
+  const dim3 grid_rows((M + kTile - 1) / kTile, H);
+  const dim3 grid_cols((N + kTile - 1) / kTile, H);
+  if (D == 128) {
+    rowsum_kernel<T, 128><<<grid_rows, RowsumCfg<128>::kThreads, RowsumCfg<128>::kSmemBytes, stream>>>(
+        mP, mV, dO, w->dsum, w->dqacc, M, N, w->status, tmo);
+    mark(1);
+    main_kernel<T, 128><<<grid_cols, MainCfg<128>::kThreads, MainCfg<128>::kSmemBytes, stream>>>(
+        mQ, mK, mV, mdO, mP, w->dsum, w->dqacc, dK, dV, M, N, w->status, tmo);
+  } else {
+    rowsum_kernel<T, 64><<<grid_rows, RowsumCfg<64>::kThreads, RowsumCfg<64>::kSmemBytes, stream>>>(
+        mP, mV, dO, w->dsum, w->dqacc, M, N, w->status, tmo);
+    mark(1);
+    main_kernel<T, 64><<<grid_cols, MainCfg<64>::kThreads, MainCfg<64>::kSmemBytes, stream>>>(
+        mQ, mK, mV, mdO, mP, w->dsum, w->dqacc, dK, dV, M, N, w->status, tmo);
+  }
+  const int64_t count = static_cast<int64_t>(rows) * D;
+  int64_t blocks = (count / 8 + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(w->sm_count > 0 ? w->sm_count : 148) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  mark(2);
+  dq_finalize_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      w->dqacc, dQ, count, w->status, w->host_status_dev);
+  mark(3);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(kErrLaunch, "launch failed: %s", cudaGetErrorString(e));
+  if (sync) {
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return set_error(kErrLaunch, "kernel failed: %s", cudaGetErrorString(e));
+    const KernelStatus st = read_status(w->host_status);
+    if (st.code != 0)
+      return set_error(kErrDeviceTimeout, "in-kernel wait gave up (code %d, site %d, block %d)",
+                       st.code, st.where, st.block);
+  }
+  return set_error(kOk, "");
+}
+
+}  // namespace fmha_sm100

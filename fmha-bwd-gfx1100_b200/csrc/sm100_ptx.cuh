@@ -1,0 +1,289 @@
+// Thin inline-PTX wrappers for the sm_100a features the attention-backward
+// kernels use: mbarriers, TMA tensor loads, tcgen05 (TMEM allocation, UMMA,
+// commit, TMEM loads) and the shared-memory matrix descriptors UMMA reads.
+//
+// Every wait on an mbarrier is bounded: a wait that does not complete within
+// the configured time sets an error code in the kernel's status word and
+// returns false, so a kernel can drain and exit instead of hanging the GPU.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace fmha_sm100 {
+
+// ----------------------------------------------------------------- status
+// Error codes written to the device status word (first writer wins).
+enum StatusCode : int {
+  kStatusOk = 0,
+  kStatusWaitTimeout = 1,   // an mbarrier wait ran out of time
+  kStatusAbortedByPeer = 2, // another role of the same CTA timed out first
+};
+
+struct KernelStatus {
+  int code;        // first error code
+  int where;       // which wait gave up (role/site id)
+  int block;       // linear block index of the first failure
+  int pad;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar,
+                                                      uint32_t bytes) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Shared per-CTA abort flag lives in shared memory; once any role gives up,
+// the others stop waiting too.
+struct WaitCtx {
+  volatile int* abort_flag;  // shared memory
+  KernelStatus* status;      // global memory
+  uint64_t timeout_ns;
+};
+
+__device__ __noinline__ void record_failure(const WaitCtx& ctx, int code,
+                                            int where) {
+  *ctx.abort_flag = 1;
+  if (atomicCAS(&ctx.status->code, 0, code) == 0) {
+    ctx.status->where = where;
+    ctx.status->block =
+        static_cast<int>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+  }
+}
+
+// Bounded wait for the phase with the given parity. Returns false (and
+// records why) if the phase does not complete within ctx.timeout_ns or if
+// another role of this CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          const WaitCtx& ctx, int where) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_test(bar, parity)) return true;
+    if ((it & 63u) == 63u) {
+      if (*ctx.abort_flag) return false;
+      if (global_timer_ns() - t0 > ctx.timeout_ns) {
+        record_failure(ctx, kStatusWaitTimeout, where);
+        return false;
+      }
+    }
+    if (it > (1u << 30)) {  // iteration cap, independent of the timer
+      record_failure(ctx, kStatusWaitTimeout, where);
+      return false;
+    }
+  }
+}
+
+// Wait used only while draining after an abort: bounded, records nothing.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity,
+                                                uint64_t timeout_ns) {
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 0; it < (1u << 28); ++it) {
+    if (mbar_test(bar, parity)) return true;
+    if ((it & 63u) == 63u && global_timer_ns() - t0 > timeout_ns) return false;
+  }
+  return false;
+}
+
+// --------------------------------------------------------------------- TMA
+__device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap))
+               : "memory");
+}
+
+// 3-D tiled TMA load (no multicast) into this CTA's shared memory; completion
+// is reported as transaction bytes on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap,
+                                            uint64_t* bar, int x, int y, int z,
+                                            uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y),
+      "r"(z), "l"(cache_hint)
+      : "memory");
+}
+
+// L2 eviction-priority hints (createpolicy.fractional with fraction 1.0).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (the tensor core reads operands through it).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ----------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile(
+      "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+          smem_u32(smem_result)),
+      "r"(ncols)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem], kind::f16 (fp16 or bf16 in, fp32 accumulate).
+__device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc,
+                                            uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive (once) on `bar` when every tcgen05 op issued so far by this thread
+// has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// Each thread of the warp reads 32 consecutive 32-bit TMEM columns of its
+// lane (lane = 32 * (warp % 4) + laneid is encoded in taddr by the caller).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+        "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+        "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]),
+        "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ------------------------------------------------------- UMMA descriptors
+// Shared-memory matrix descriptor (tcgen05 format):
+//   [0,14)  start address >> 4
+//   [16,30) leading-dimension byte offset >> 4
+//   [32,46) stride-dimension byte offset >> 4
+//   [46,48) version = 1
+//   [49,52) base offset = 0 (tiles are 1024-byte aligned)
+//   [52]    LBO mode = 0
+//   [61,64) layout: 2 = 128-byte swizzle
+// With 128-byte swizzle, a K-major operand is rows of 128 bytes grouped in
+// 8-row (1024-byte) atoms: SBO = 1024, LBO unused. An MN-major operand is
+// 64-element (128-byte) MN runs, 8 K-rows per atom: SBO = 1024 between K
+// groups of 8, LBO = distance between consecutive 64-element MN blocks.
+__device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr,
+                                                    uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with fp32 accumulation.
+//   [4,6) D format (1 = F32); [7,10) A format; [10,13) B format
+//   (0 = F16, 1 = BF16); [15] A MN-major; [16] B MN-major;
+//   [17,23) N >> 3; [24,29) M >> 4.
+template <bool kBF16>
+__host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool a_mn_major,
+                                                      bool b_mn_major) {
+  return (1u << 4) | ((kBF16 ? 1u : 0u) << 7) | ((kBF16 ? 1u : 0u) << 10) |
+         ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((static_cast<uint32_t>(N) >> 3) << 17) |
+         ((static_cast<uint32_t>(M) >> 4) << 24);
+}
+
+// ------------------------------------------------------------ misc helpers
+__device__ __forceinline__ void red_add_v4_f32(float* gaddr, float a, float b,
+                                               float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gaddr), "f"(a),
+               "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t lane_id() {
+  uint32_t l;
+  asm volatile("mov.u32 %0, %%laneid;" : "=r"(l));
+  return l;
+}
+
+}  // namespace fmha_sm100

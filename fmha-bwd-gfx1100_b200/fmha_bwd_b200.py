@@ -1,0 +1,214 @@
+"""Host-side mirror of the reference's Python/ctypes interface for the
+attention-backward path, backed by the sm_100a libraries in build/.
+
+Reference interface (benchmark_pytorch_final.py):
+  * ``lib = ctypes.CDLL('./build/libfmha_bwd_bf16.so')`` with argtypes of
+    8 x c_void_p + 4 x c_int (:30-37)
+  * ``custom_flash_attn_backward(Q, K, V, P, dO)`` (:39-53): zero-fills the
+    outputs and calls ``fmha_bwd_full_py`` with device pointers
+  * ``pytorch_naive_backward`` (:58-70): einsum reference (no scale)
+  * ``benchmark_size(batch, heads, M, N, K_dim, ...)`` (:82-136)
+
+This module keeps those names, argument meanings and return values. It
+differs from the reference script in three deliberate ways:
+  * ``total_heads`` is ``batch * heads`` (the reference passes ``heads``,
+    :51, which only covers batch 1);
+  * the library is chosen by dtype (bf16 -> libfmha_bwd_bf16.so, fp16 ->
+    libfmha_bwd_fp16.so) instead of always loading the bf16 one;
+  * a call the library rejects raises ``FmhaBwdError`` with the library's
+    error code and message instead of silently returning zeros.
+
+There is no fallback: if the CUDA library is missing or the device is not an
+sm_100 GPU, calls raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+ROOT_DIR = os.path.dirname(PKG_DIR)
+BUILD_DIR = os.path.join(ROOT_DIR, "build")
+
+LIB_NAMES = {
+    torch.bfloat16: ("libfmha_bwd_bf16.so", "fmha_bwd_full_py", "fmha_bwd_full_stream"),
+    torch.float16: ("libfmha_bwd_fp16.so", "fmha_bwd_full_fp16", "fmha_bwd_full_fp16_stream"),
+}
+
+ERROR_NAMES = {
+    0: "OK",
+    1: "INVALID_ARGUMENT",
+    2: "MISALIGNED",
+    3: "UNSUPPORTED_DEVICE",
+    4: "OUT_OF_MEMORY",
+    5: "LAUNCH",
+    6: "DEVICE_TIMEOUT",
+    7: "NO_DRIVER",
+}
+
+
+class FmhaBwdError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"fmha_bwd error {code} ({ERROR_NAMES.get(code, '?')}): {message}")
+        self.code = code
+
+
+_LIBS: dict[str, ctypes.CDLL] = {}
+
+_PTR_ARGS = [ctypes.c_void_p] * 8
+_INT_ARGS = [ctypes.c_int] * 4
+
+
+def library_path(dtype: torch.dtype) -> str:
+    if dtype not in LIB_NAMES:
+        raise TypeError(f"unsupported dtype {dtype}; use torch.bfloat16 or torch.float16")
+    return os.path.join(BUILD_DIR, LIB_NAMES[dtype][0])
+
+
+def load_library(dtype: torch.dtype = torch.bfloat16) -> ctypes.CDLL:
+    """Load (once) and return the ctypes handle for ``dtype``'s library, with
+    the same argtypes the reference script declares (:32-37)."""
+    path = library_path(dtype)
+    lib = _LIBS.get(path)
+    if lib is not None:
+        return lib
+    if not os.path.exists(path):
+        raise FileNotFoundError(
+            f"{path} is missing: build it with python fmha-bwd-gfx1100_b200/build_libs.py")
+    lib = ctypes.CDLL(path)
+    _, full, stream = LIB_NAMES[dtype]
+    getattr(lib, full).argtypes = _PTR_ARGS + _INT_ARGS
+    getattr(lib, full).restype = None
+    getattr(lib, stream).argtypes = _PTR_ARGS + _INT_ARGS + [ctypes.c_void_p]
+    getattr(lib, stream).restype = ctypes.c_int
+    lib.fmha_bwd_last_error.argtypes = []
+    lib.fmha_bwd_last_error.restype = ctypes.c_int
+    lib.fmha_bwd_last_error_message.argtypes = []
+    lib.fmha_bwd_last_error_message.restype = ctypes.c_char_p
+    lib.fmha_bwd_poll_device_status.argtypes = []
+    lib.fmha_bwd_poll_device_status.restype = ctypes.c_int
+    lib.fmha_bwd_set_wait_timeout_ms.argtypes = [ctypes.c_int]
+    lib.fmha_bwd_set_wait_timeout_ms.restype = None
+    _LIBS[path] = lib
+    return lib
+
+
+def last_error(dtype: torch.dtype = torch.bfloat16) -> tuple[int, str]:
+    lib = load_library(dtype)
+    return lib.fmha_bwd_last_error(), (lib.fmha_bwd_last_error_message() or b"").decode()
+
+
+def _raise_if_error(lib: ctypes.CDLL, rc: int | None = None) -> None:
+    code = lib.fmha_bwd_last_error() if rc is None else rc
+    if code != 0:
+        msg = (lib.fmha_bwd_last_error_message() or b"").decode()
+        raise FmhaBwdError(code, msg)
+
+
+def _check_inputs(Q, K, V, P, dO):
+    for name, t in (("Q", Q), ("K", K), ("V", V), ("P", P), ("dO", dO)):
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+        if t.dtype != Q.dtype:
+            raise TypeError(f"{name} has dtype {t.dtype}, expected {Q.dtype}")
+
+
+def fmha_bwd(Q, K, V, P, dO, *, out=None, stream=None, sync: bool = True):
+    """Backward of attention for head-flattened tensors.
+
+    Q, dO: [H, M, d]; K, V: [H, N, d]; P: [H, M, N] (any leading shape that
+    flattens to these, contiguous). Returns (dQ, dK, dV) with the shapes of
+    Q, K, V. ``out`` may supply preallocated (dQ, dK, dV) tensors, which are
+    fully overwritten. With ``sync=True`` the call uses the reference entry
+    (``fmha_bwd_full_py`` / ``fmha_bwd_full_fp16``), which returns after the
+    work has finished; with ``sync=False`` it uses the stream-ordered entry
+    on ``stream`` (default: torch's current stream) and returns at once.
+    """
+    _check_inputs(Q, K, V, P, dO)
+    d = Q.shape[-1]
+    M = Q.shape[-2]
+    N = K.shape[-2]
+    H = Q.numel() // (M * d)
+    if K.numel() != H * N * d or V.numel() != H * N * d or dO.numel() != H * M * d \
+            or P.numel() != H * M * N:
+        raise ValueError("inconsistent shapes for Q, K, V, P, dO")
+    lib = load_library(Q.dtype)
+    if out is None:
+        dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
+    else:
+        dQ, dK, dV = out
+    args = (dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), Q.data_ptr(), K.data_ptr(),
+            V.data_ptr(), P.data_ptr(), dO.data_ptr(), M, N, d, H)
+    _, full, stream_fn = LIB_NAMES[Q.dtype]
+    if sync:
+        getattr(lib, full)(*args)
+        _raise_if_error(lib)
+    else:
+        s = stream if stream is not None else torch.cuda.current_stream(Q.device)
+        rc = getattr(lib, stream_fn)(*args, ctypes.c_void_p(s.cuda_stream))
+        _raise_if_error(lib, rc)
+    return dQ, dK, dV
+
+
+def custom_flash_attn_backward(Q, K, V, P, dO):
+    """Mirror of the reference's custom_flash_attn_backward
+    (benchmark_pytorch_final.py:39-53) for [batch, heads, M, d] inputs.
+    Outputs are zero-filled first, as the reference does (:43-45), then fully
+    overwritten by the library."""
+    batch, heads, M, K_dim = Q.shape
+    dQ = torch.zeros_like(Q)
+    dK = torch.zeros_like(K)
+    dV = torch.zeros_like(V)
+    return fmha_bwd(Q, K, V, P, dO, out=(dQ, dK, dV))
+
+
+def pytorch_naive_backward(Q, K, V, P, dO):
+    """The reference script's einsum formula (benchmark_pytorch_final.py:58-70),
+    computed here in fp32 on the inputs' device. Test/benchmark reference only."""
+    Qf, Kf, Vf, Pf, dOf = (t.float() for t in (Q, K, V, P, dO))
+    dP = torch.einsum("...mk,...nk->...mn", dOf, Vf)
+    rowsum = (dP * Pf).sum(dim=-1, keepdim=True)
+    dS = Pf * (dP - rowsum)
+    dQ = torch.einsum("...mn,...nk->...mk", dS, Kf)
+    dK = torch.einsum("...mn,...mk->...nk", dS, Qf)
+    dV = torch.einsum("...mn,...mk->...nk", Pf, dOf)
+    return dQ, dK, dV
+
+
+def benchmark_size(batch, heads, M, N, K_dim, dtype=torch.bfloat16, warmup=5, reps=20):
+    """Mirror of the reference's benchmark_size (benchmark_pytorch_final.py:82-136):
+    seeded inputs, warmup, CUDA-event timing of ``reps`` synchronous calls,
+    FLOPs = 4 * 2*M*N*d per head (:125-127, here summed over batch*heads),
+    and the max difference against the einsum reference."""
+    device = torch.device("cuda")
+    torch.manual_seed(42)
+    Q = torch.randn(batch, heads, M, K_dim, dtype=dtype, device=device)
+    K = torch.randn(batch, heads, N, K_dim, dtype=dtype, device=device)
+    V = torch.randn(batch, heads, N, K_dim, dtype=dtype, device=device)
+    dO = torch.randn(batch, heads, M, K_dim, dtype=dtype, device=device)
+    P = torch.softmax(torch.randn(batch, heads, M, N, dtype=dtype, device=device), dim=-1)
+    for _ in range(warmup):
+        custom_flash_attn_backward(Q, K, V, P, dO)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        dQ, dK, dV = custom_flash_attn_backward(Q, K, V, P, dO)
+    end.record()
+    torch.cuda.synchronize()
+    custom_ms = start.elapsed_time(end) / reps
+    rQ, rK, rV = pytorch_naive_backward(Q, K, V, P, dO)
+    max_diff = max((dQ.float() - rQ).abs().max().item(), (dK.float() - rK).abs().max().item(),
+                   (dV.float() - rV).abs().max().item())
+    flops = 4 * 2.0 * M * N * K_dim * batch * heads
+    return {
+        "M": M, "N": N, "K": K_dim,
+        "custom_time_ms": custom_ms,
+        "max_diff": max_diff,
+        "custom_tflops": flops / (custom_ms * 1e-3) / 1e12 if custom_ms > 0 else 0.0,
+    }

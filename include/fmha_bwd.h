@@ -1,0 +1,138 @@
+/* C-ABI of the B200 (sm_100a) attention-backward libraries.
+ *
+ *   build/libfmha_bwd_bf16.so  exports the bf16 entry points
+ *   build/libfmha_bwd_fp16.so  exports the fp16 entry points
+ *
+ * Both libraries are drop-in replacements for the reference's
+ * build/libfmha_bwd_bf16.so / build/libfmha_bwd_fp16.so: the ctypes host in
+ * benchmark_pytorch_final.py:30-37 loads them and calls them unchanged.
+ *
+ * Semantics (no softmax scale; src/kernel/correct/cpu_reference.hpp:30-40,
+ * :74-126), for every head h:
+ *   dP = dO V^T;  D = rowsum(P * dP);  dS = P * (dP - D)
+ *   dQ = dS K;    dK = dS^T Q;          dV = P^T dO
+ * Layout per head h (row-major, heads contiguous): Q, dO, dQ at h*M*K_dim;
+ * K, V, dK, dV at h*N*K_dim; P at h*M*N (src/fmha_bwd_kernels.hip:72-74).
+ * Inputs are read only; dQ, dK and dV are fully overwritten.
+ *
+ * Preconditions (checked before anything is launched; on failure nothing is
+ * written, a message goes to stderr and fmha_bwd_last_error() is non-zero):
+ *   M, N, total_heads > 0; K_dim is 64 or 128; total_heads <= 65535;
+ *   N % 8 == 0 (each P row starts on a 16-byte boundary);
+ *   every pointer is 16-byte aligned device memory of the current device,
+ *   which must be an sm_100 GPU.
+ *
+ * Storage types are 16-bit; the C side sees them as uint16_t.
+ */
+#ifndef FMHA_BWD_B200_H_
+#define FMHA_BWD_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint16_t fmha_bf16_t; /* bfloat16 bits */
+typedef uint16_t fmha_fp16_t; /* IEEE half bits */
+typedef struct CUstream_st* fmha_stream_t; /* cudaStream_t */
+
+/* Error codes (fmha_bwd_last_error). */
+enum {
+  FMHA_BWD_OK = 0,
+  FMHA_BWD_ERR_INVALID_ARGUMENT = 1,
+  FMHA_BWD_ERR_MISALIGNED = 2,
+  FMHA_BWD_ERR_UNSUPPORTED_DEVICE = 3,
+  FMHA_BWD_ERR_OUT_OF_MEMORY = 4,
+  FMHA_BWD_ERR_LAUNCH = 5,
+  FMHA_BWD_ERR_DEVICE_TIMEOUT = 6,
+  FMHA_BWD_ERR_NO_DRIVER = 7
+};
+
+/* ---- libfmha_bwd_bf16.so ------------------------------------------------ */
+
+/* Replaces fmha_bwd_full_py, src/fmha_bwd_kernels.hip:474-477 (bf16).
+ * Launches on the legacy default stream and returns after that stream has
+ * finished, like the reference (which ends with hipDeviceSynchronize, :520). */
+void fmha_bwd_full_py(fmha_bf16_t* dQ, fmha_bf16_t* dK, fmha_bf16_t* dV,
+                      const fmha_bf16_t* Q, const fmha_bf16_t* K,
+                      const fmha_bf16_t* V, const fmha_bf16_t* P,
+                      const fmha_bf16_t* dO, int M, int N, int K_dim,
+                      int total_heads);
+
+/* Stream-ordered variant (the reference's stale header imagines a stream
+ * argument for fmha_bwd_full, src/fmha_bwd_kernels.hpp:60-65). Enqueues the
+ * work on `stream` and returns at once with 0, or an error code if the call
+ * was rejected before launch. Calls on different streams of one device must
+ * not overlap: they share the device's workspace. */
+int fmha_bwd_full_stream(fmha_bf16_t* dQ, fmha_bf16_t* dK, fmha_bf16_t* dV,
+                         const fmha_bf16_t* Q, const fmha_bf16_t* K,
+                         const fmha_bf16_t* V, const fmha_bf16_t* P,
+                         const fmha_bf16_t* dO, int M, int N, int K_dim,
+                         int total_heads, fmha_stream_t stream);
+
+/* Profiling variant of fmha_bwd_full_stream: additionally records the four
+ * CUDA events in `events` (cudaEvent_t[4], entries may be NULL) on `stream`
+ * before the rowsum kernel, before the main kernel, before the dQ finalize
+ * kernel and after it, so a caller can time each kernel inside a run.
+ * No counterpart in the reference. */
+int fmha_bwd_full_stream_events(fmha_bf16_t* dQ, fmha_bf16_t* dK,
+                                fmha_bf16_t* dV, const fmha_bf16_t* Q,
+                                const fmha_bf16_t* K, const fmha_bf16_t* V,
+                                const fmha_bf16_t* P, const fmha_bf16_t* dO,
+                                int M, int N, int K_dim, int total_heads,
+                                fmha_stream_t stream, void* const* events);
+
+/* ---- libfmha_bwd_fp16.so ------------------------------------------------ */
+
+/* Replaces fmha_bwd_full_fp16, src/fmha_bwd_kernels_fp16.hip:236-238. */
+void fmha_bwd_full_fp16(fmha_fp16_t* dQ, fmha_fp16_t* dK, fmha_fp16_t* dV,
+                        const fmha_fp16_t* Q, const fmha_fp16_t* K,
+                        const fmha_fp16_t* V, const fmha_fp16_t* P,
+                        const fmha_fp16_t* dO, int M, int N, int K_dim,
+                        int total_heads);
+
+/* fp16 stream-ordered variant, as fmha_bwd_full_stream. */
+int fmha_bwd_full_fp16_stream(fmha_fp16_t* dQ, fmha_fp16_t* dK,
+                              fmha_fp16_t* dV, const fmha_fp16_t* Q,
+                              const fmha_fp16_t* K, const fmha_fp16_t* V,
+                              const fmha_fp16_t* P, const fmha_fp16_t* dO,
+                              int M, int N, int K_dim, int total_heads,
+                              fmha_stream_t stream);
+
+/* fp16 profiling variant, as fmha_bwd_full_stream_events. */
+int fmha_bwd_full_fp16_stream_events(fmha_fp16_t* dQ, fmha_fp16_t* dK,
+                                     fmha_fp16_t* dV, const fmha_fp16_t* Q,
+                                     const fmha_fp16_t* K, const fmha_fp16_t* V,
+                                     const fmha_fp16_t* P, const fmha_fp16_t* dO,
+                                     int M, int N, int K_dim, int total_heads,
+                                     fmha_stream_t stream, void* const* events);
+
+/* ---- exported by both libraries ---------------------------------------- */
+
+/* Additive to the reference (whose entry returns void and only prints on
+ * allocation failure, src/fmha_bwd_kernels.hip:486-490): the code of the most
+ * recent call in this process (FMHA_BWD_OK if it succeeded). For the stream
+ * variants, in-kernel wait timeouts are reported by the next synchronous call
+ * or by fmha_bwd_poll_device_status() after the stream has finished. */
+int fmha_bwd_last_error(void);
+
+/* Human-readable message for the most recent error ("" if none). */
+const char* fmha_bwd_last_error_message(void);
+
+/* Reads the device status word written by the most recently completed call
+ * on the current device: 0 if every in-kernel wait completed, else
+ * FMHA_BWD_ERR_DEVICE_TIMEOUT. Call after synchronising the stream. */
+int fmha_bwd_poll_device_status(void);
+
+/* Upper bound, in milliseconds, on any single in-kernel wait (default 4000,
+ * or FMHA_BWD_WAIT_TIMEOUT_MS). A wait that runs out sets the device status
+ * word and the kernel drains and exits instead of hanging. 0 restores the
+ * default. */
+void fmha_bwd_set_wait_timeout_ms(int ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FMHA_BWD_B200_H_ */

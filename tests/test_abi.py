@@ -1,0 +1,123 @@
+"""CPU tests of the C-ABI boundary: both libraries load, export every entry
+point include/fmha_bwd.h declares, and reject bad calls before touching the
+GPU (so these run without one)."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "fmha_bwd.h")
+LIBS = {
+    "bf16": os.path.join(ROOT, "build", "libfmha_bwd_bf16.so"),
+    "fp16": os.path.join(ROOT, "build", "libfmha_bwd_fp16.so"),
+}
+
+
+def _ensure_built():
+    if not all(os.path.exists(p) for p in LIBS.values()):
+        import build_libs
+
+        build_libs.build()
+
+
+def header_functions():
+    """{section: [function names]} from the header's ---- section markers."""
+    text = open(HEADER).read()
+    sections = {"bf16": [], "fp16": [], "both": []}
+    current = None
+    for line in text.splitlines():
+        if "---- libfmha_bwd_bf16.so" in line:
+            current = "bf16"
+        elif "---- libfmha_bwd_fp16.so" in line:
+            current = "fp16"
+        elif "---- exported by both libraries" in line:
+            current = "both"
+        m = re.match(r"^\s*(?:void|int|const char\s*\*)\s+(\w+)\s*\(", line)
+        if m and current:
+            sections[current].append(m.group(1))
+    return sections
+
+
+def exported(path):
+    out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True,
+                         check=True).stdout
+    return {l.split()[-1] for l in out.splitlines() if l.strip()}
+
+
+def test_header_declares_reference_entry_points():
+    s = header_functions()
+    assert "fmha_bwd_full_py" in s["bf16"]
+    assert "fmha_bwd_full_fp16" in s["fp16"]
+    assert "fmha_bwd_last_error" in s["both"]
+
+
+@pytest.mark.parametrize("kind", ["bf16", "fp16"])
+def test_library_exports_every_declared_symbol(kind):
+    _ensure_built()
+    s = header_functions()
+    want = set(s[kind]) | set(s["both"])
+    have = exported(LIBS[kind])
+    assert want <= have, f"missing exports: {sorted(want - have)}"
+    lib = ctypes.CDLL(LIBS[kind])
+    for name in want:
+        assert getattr(lib, name) is not None
+
+
+def _call_full(lib, fn, ptrs, M, N, d, H):
+    f = getattr(lib, fn)
+    f.argtypes = [ctypes.c_void_p] * 8 + [ctypes.c_int] * 4
+    f.restype = None
+    f(*ptrs, M, N, d, H)
+    lib.fmha_bwd_last_error.restype = ctypes.c_int
+    lib.fmha_bwd_last_error_message.restype = ctypes.c_char_p
+    return lib.fmha_bwd_last_error(), lib.fmha_bwd_last_error_message().decode()
+
+
+@pytest.mark.parametrize("kind,fn", [("bf16", "fmha_bwd_full_py"), ("fp16", "fmha_bwd_full_fp16")])
+def test_rejects_bad_arguments_without_gpu(kind, fn):
+    """Preconditions are checked on the host before any CUDA call; each bad
+    call returns the documented error code (no GPU needed)."""
+    _ensure_built()
+    lib = ctypes.CDLL(LIBS[kind])
+    good = [0x10000 * (i + 1) for i in range(8)]  # never dereferenced: rejected earlier
+    code, msg = _call_full(lib, fn, [None] + good[1:], 128, 128, 64, 2)
+    assert code == 1 and "null" in msg
+    code, _ = _call_full(lib, fn, good, 0, 128, 64, 2)
+    assert code == 1
+    code, _ = _call_full(lib, fn, good, 128, -5, 64, 2)
+    assert code == 1
+    code, msg = _call_full(lib, fn, good, 128, 128, 96, 2)
+    assert code == 1 and "K_dim" in msg
+    code, _ = _call_full(lib, fn, good, 128, 128, 64, 0)
+    assert code == 1
+    code, msg = _call_full(lib, fn, good, 128, 130, 64, 2)
+    assert code == 2
+    code, msg = _call_full(lib, fn, [p + 2 for p in good], 128, 128, 64, 2)
+    assert code == 2 and "aligned" in msg
+
+
+def test_stream_entry_rejects_with_return_code():
+    _ensure_built()
+    lib = ctypes.CDLL(LIBS["bf16"])
+    f = lib.fmha_bwd_full_stream
+    f.argtypes = [ctypes.c_void_p] * 8 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    f.restype = ctypes.c_int
+    assert f(*([None] * 8), 128, 128, 64, 2, None) == 1
+
+
+def test_python_mirror_fails_loudly_without_cuda_tensors():
+    import torch
+
+    import fmha_bwd_b200 as F
+
+    x = torch.zeros(1, 128, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        F.fmha_bwd(x, x, x, torch.zeros(1, 128, 128, dtype=torch.bfloat16), x)
+    with pytest.raises(TypeError):
+        F.library_path(torch.float32)
