@@ -178,6 +178,13 @@ def run_reference_arm(args, w):
         return 0
     threads = cpu_threads(w)
     rows = args.cpu_rows_per_step
+    if rows <= 0:
+        # size each step so the whole run (warm-up + timed) takes ~2 minutes
+        fl, dt, _, _ = cpu_reference_sample(w, 16, threads)
+        per_row = dt / 16.0
+        budget = 120.0 / max(1, args.steps + args.warmup)
+        rows = int(budget / max(per_row, 1e-9)) // 8 * 8
+        rows = max(8, min(rows, 1024, w.M))
     for _ in range(args.warmup):
         cpu_reference_sample(w, rows, threads)
     times, flops, kind = [], 0.0, "reference"
@@ -211,7 +218,7 @@ def run_reference_arm(args, w):
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="flux")
@@ -219,8 +226,9 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=512,
                     help="query rows per head in the CPU baseline sample")
-    ap.add_argument("--cpu-rows-per-step", type=int, default=128,
-                    help="query rows per head per step of the reference arm")
+    ap.add_argument("--cpu-rows-per-step", type=int, default=0,
+                    help="query rows per head per step of the reference arm "
+                         "(0: sized so the run takes about two minutes)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -280,6 +288,10 @@ def main() -> int:
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K_steps)]
     ev_arrays = []
     for e4 in evs:
+        for e in e4:
+            e.record(stream)  # torch creates the CUDA event lazily, at first record
+        if any(not e.cuda_event for e in e4):
+            raise RuntimeError("could not create CUDA timing events")
         arr = (ctypes.c_void_p * 4)(*[e.cuda_event for e in e4])
         ev_arrays.append(arr)
     start = torch.cuda.Event(enable_timing=True)

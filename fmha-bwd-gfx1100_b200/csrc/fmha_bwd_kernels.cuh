@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(RowsumCfg<D>::kThreads, 1)
     const int r = q * 32 + lane;
     const int m = m0 + r;
     const bool ok = mbar_wait(o_full, 0, ctx, 3);
+    __syncwarp();  // lanes leave the wait loop independently; tcgen05.ld is .aligned
     if (ok) {
       tc_fence_after();
       float acc = 0.f;
@@ -212,8 +213,7 @@ __global__ void __launch_bounds__(RowsumCfg<D>::kThreads, 1)
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, v);
-        tmem_ld_wait();
+        tmem_load_32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, v);
         if (m < M) {
           const uint4* src = reinterpret_cast<const uint4*>(dO_row + c * 32);
 #pragma unroll
@@ -249,8 +249,23 @@ __global__ void __launch_bounds__(RowsumCfg<D>::kThreads, 1)
 
 // --------------------------------------------------------------- main
 // Shared-memory plan (D = 128): K_j 32 KB, V_j 32 KB, P_ij x2 64 KB, dS 32 KB,
-// dO_i 32 KB, Q_i 32 KB = 224 KB. TMEM (512 columns): dP [0,128), dV
-// [128,128+D), dK [128+D,128+2D), dQ [128+2D,128+3D).
+// dO_i 32 KB, Q_i 32 KB = 224 KB.
+// TMEM (512 columns): dP [0,128) (lane = query row, column = key),
+// dV [128,128+D) and dK [128+D,128+2D) (lane = key row, column = d), and the
+// dQ partial at [128+2D, ...):
+//   D = 128: dQ^T = K_j^T dS^T, lane = d, column = query row (128 columns),
+//            so each warp reduces 32 consecutive floats of one dQ row per
+//            instruction (one 128-byte line);
+//   D = 64:  dQ = dS K_j, lane = query row, column = d (64 columns).
+//
+// Warp roles (20 warps): 0 TMA for K_j, V_j and the P stream; 1 MMA issuer
+// for dP and dV (and TMEM owner); 2 TMA for dO_i and Q_i; 3 MMA issuer for
+// dK and dQ; 4-11 dS warps (TMEM lane
+// quarter = warp % 4, column half = (warp - 4) / 4), which also write the
+// final dK_j, dV_j; 12-19 dQ warps (lane quarter = warp % 4, column half =
+// (warp - 12) / 4). A dQ warp first copies its 64 TMEM columns of the dQ
+// partial into registers and releases the TMEM, then issues the global
+// reductions, so the reduction traffic never holds up the next dQ MMA.
 template <int D>
 struct MainCfg {
   static constexpr int kMD = (D / kBoxCols) * kBoxBytes;  // one [128 x D] tile
@@ -264,14 +279,19 @@ struct MainCfg {
   static constexpr int kTileBytes = kOffQ + kMD;
   static constexpr int kBarBytes = 256;
   static constexpr int kSmemBytes = kTileBytes + kBarBytes + 1024;
-  static constexpr int kEpiWarps = 8;
-  static constexpr int kThreads = 32 * (3 + kEpiWarps);  // TMA-P, MMA, TMA-Q/dO, 8 epilogue
+  static constexpr int kDSWarps = 8;
+  static constexpr int kDQWarps = 8;
+  static constexpr int kFirstDSWarp = 4;
+  static constexpr int kFirstDQWarp = kFirstDSWarp + kDSWarps;
+  static constexpr int kThreads = 32 * (kFirstDQWarp + kDQWarps);
+  static constexpr bool kDQTransposed = (D == 128);
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kColdP = 0;
   static constexpr uint32_t kColdV = 128;
   static constexpr uint32_t kColdK = 128 + D;
   static constexpr uint32_t kColdQ = 128 + 2 * D;
-  static_assert(kColdQ + D <= kTmemCols, "TMEM budget");
+  static constexpr uint32_t kdQCols = kDQTransposed ? kTile : D;
+  static_assert(kColdQ + kdQCols <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -294,8 +314,26 @@ enum MainBar : int {
   kBarDQEmpty = 14,
   kBarAccFull = 15,
   kBarDrain = 16,
-  kNumMainBars = 17,
+  kBarDrain2 = 17,
+  kNumMainBars = 18,
 };
+
+// dS for 8 consecutive keys of one row: P (8 x 16-bit, one 16-byte chunk)
+// times (dP - D), packed back to 16-bit.
+template <typename T>
+__device__ __forceinline__ uint4 ds_chunk(uint4 pv, const uint32_t* dp, float Dm) {
+  const float2 nD = make_float2(-Dm, -Dm);
+  const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const float2 p = Elem<T>::unpack(pw[t]);
+    const float2 g = make_float2(__uint_as_float(dp[2 * t]), __uint_as_float(dp[2 * t + 1]));
+    const float2 r = mul_f32x2(p, add_f32x2(g, nD));
+    o[t] = Elem<T>::pack(r.x, r.y);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(MainCfg<D>::kThreads, 1)
@@ -307,7 +345,6 @@ __global__ void __launch_bounds__(MainCfg<D>::kThreads, 1)
                 float* __restrict__ dQacc, T* __restrict__ dK, T* __restrict__ dV, int M,
                 int N, KernelStatus* status, uint64_t timeout_ns) {
   using Cfg = MainCfg<D>;
-  constexpr int kEpi = Cfg::kEpiWarps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -325,20 +362,21 @@ __global__ void __launch_bounds__(MainCfg<D>::kThreads, 1)
     mbar_init(&bar[kBarKV], 1);
     mbar_init(&bar[kBarPFull0], 1);
     mbar_init(&bar[kBarPFull1], 1);
-    mbar_init(&bar[kBarPEmpty0], 1 + kEpi);
-    mbar_init(&bar[kBarPEmpty1], 1 + kEpi);
+    mbar_init(&bar[kBarPEmpty0], 1 + Cfg::kDSWarps);
+    mbar_init(&bar[kBarPEmpty1], 1 + Cfg::kDSWarps);
     mbar_init(&bar[kBarDOFull], 1);
     mbar_init(&bar[kBarDOEmpty], 1);
     mbar_init(&bar[kBarQFull], 1);
     mbar_init(&bar[kBarQEmpty], 1);
     mbar_init(&bar[kBarDPFull], 1);
-    mbar_init(&bar[kBarDPEmpty], kEpi);
-    mbar_init(&bar[kBarDSFull], kEpi);
+    mbar_init(&bar[kBarDPEmpty], Cfg::kDSWarps);
+    mbar_init(&bar[kBarDSFull], Cfg::kDSWarps);
     mbar_init(&bar[kBarDSEmpty], 1);
     mbar_init(&bar[kBarDQFull], 1);
-    mbar_init(&bar[kBarDQEmpty], kEpi);
-    mbar_init(&bar[kBarAccFull], 1);
+    mbar_init(&bar[kBarDQEmpty], Cfg::kDQWarps);
+    mbar_init(&bar[kBarAccFull], 2);
     mbar_init(&bar[kBarDrain], 1);
+    mbar_init(&bar[kBarDrain2], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -384,40 +422,76 @@ __global__ void __launch_bounds__(MainCfg<D>::kThreads, 1)
       }
     }
   } else if (warp == 2) {
-    // ---- TMA producer: dO_i and Q_i (single-buffered, L2-resident).
+    // ---- TMA producer for the L2-resident operands dO_i and Q_i
+    // (single-buffered each). It polls both "empty" barriers without
+    // blocking and issues whichever load can go, so neither stream waits
+    // behind the other. Tiles are first prefetched into L2 kL2Ahead query
+    // tiles ahead (they are shared by every key-tile CTA of the head).
     if (lane == 0) {
+      constexpr int kL2Ahead = 3;
       tma_prefetch_desc(&tm_dO);
       tma_prefetch_desc(&tm_Q);
       const uint64_t pol = l2_policy_evict_last();
-      int issued_do = 0, issued_q = 0;
-      for (int i = 0; i < mt; ++i) {
-        if (i > 0 && !mbar_wait(&bar[kBarDOEmpty], (i - 1) & 1, ctx, 20)) break;
-        mbar_arrive_expect_tx(&bar[kBarDOFull], Cfg::kMD);
+      for (int i = 0; i < kL2Ahead && i < mt; ++i)
+        for (int b = 0; b < D / kBoxCols; ++b) {
+          tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, i * kTile, h);
+          tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, i * kTile, h);
+        }
+      int next_do = 0, next_q = 0;
+      uint64_t t_last = global_timer_ns();
+      bool failed = false;
+      while ((next_do < mt || next_q < mt) && !failed) {
+        bool progressed = false;
+        if (next_do < mt && (next_do == 0 || mbar_test(&bar[kBarDOEmpty], (next_do - 1) & 1))) {
+          mbar_arrive_expect_tx(&bar[kBarDOFull], Cfg::kMD);
 #pragma unroll
-        for (int b = 0; b < D / kBoxCols; ++b)
-          tma_load_3d(smem + Cfg::kOffdO + b * kBoxBytes, &tm_dO, &bar[kBarDOFull], b * kBoxCols,
-                      i * kTile, h, pol);
-        ++issued_do;
-        if (i > 0 && !mbar_wait(&bar[kBarQEmpty], (i - 1) & 1, ctx, 21)) break;
-        mbar_arrive_expect_tx(&bar[kBarQFull], Cfg::kMD);
+          for (int b = 0; b < D / kBoxCols; ++b)
+            tma_load_3d(smem + Cfg::kOffdO + b * kBoxBytes, &tm_dO, &bar[kBarDOFull], b * kBoxCols,
+                        next_do * kTile, h, pol);
+          if (next_do + kL2Ahead < mt)
+            for (int b = 0; b < D / kBoxCols; ++b)
+              tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, (next_do + kL2Ahead) * kTile, h);
+          ++next_do;
+          progressed = true;
+        }
+        if (next_q < mt && (next_q == 0 || mbar_test(&bar[kBarQEmpty], (next_q - 1) & 1))) {
+          mbar_arrive_expect_tx(&bar[kBarQFull], Cfg::kMD);
 #pragma unroll
-        for (int b = 0; b < D / kBoxCols; ++b)
-          tma_load_3d(smem + Cfg::kOffQ + b * kBoxBytes, &tm_Q, &bar[kBarQFull], b * kBoxCols,
-                      i * kTile, h, pol);
-        ++issued_q;
+          for (int b = 0; b < D / kBoxCols; ++b)
+            tma_load_3d(smem + Cfg::kOffQ + b * kBoxBytes, &tm_Q, &bar[kBarQFull], b * kBoxCols,
+                        next_q * kTile, h, pol);
+          if (next_q + kL2Ahead < mt)
+            for (int b = 0; b < D / kBoxCols; ++b)
+              tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, (next_q + kL2Ahead) * kTile, h);
+          ++next_q;
+          progressed = true;
+        }
+        if (progressed) {
+          t_last = global_timer_ns();
+        } else {
+          if (*abort_flag) break;
+          if (global_timer_ns() - t_last > timeout_ns) {
+            record_failure(ctx, kStatusWaitTimeout, 20);
+            failed = true;
+          }
+        }
       }
       if (*abort_flag) {
-        if (issued_do > 0) mbar_wait_drain(&bar[kBarDOFull], (issued_do - 1) & 1, timeout_ns);
-        if (issued_q > 0) mbar_wait_drain(&bar[kBarQFull], (issued_q - 1) & 1, timeout_ns);
+        if (next_do > 0) mbar_wait_drain(&bar[kBarDOFull], (next_do - 1) & 1, timeout_ns);
+        if (next_q > 0) mbar_wait_drain(&bar[kBarQFull], (next_q - 1) & 1, timeout_ns);
       }
     }
-  } else if (warp == 1) {
-    // ---- MMA issuer (one thread).
+  } else if (warp == 1 || warp == 3) {
+    // ---- MMA issuers: warp 1 issues dP and dV, warp 3 issues dK and dQ.
+    // Two issuing threads keep the tensor pipe fed while either one waits.
     if (lane == 0) {
       constexpr bool kB = Elem<T>::kBF16;
       constexpr uint32_t id_dP = make_idesc_f16<kB>(kTile, kTile, false, false);
       constexpr uint32_t id_dVK = make_idesc_f16<kB>(kTile, D, true, true);
-      constexpr uint32_t id_dQ = make_idesc_f16<kB>(kTile, D, false, true);
+      // D = 128: dQ^T (M = d, N = query rows; A = K_j^T MN-major, B = dS^T K-major).
+      // D = 64:  dQ   (M = query rows, N = d; A = dS K-major, B = K_j MN-major).
+      constexpr uint32_t id_dQ = Cfg::kDQTransposed ? make_idesc_f16<kB>(kTile, kTile, true, false)
+                                                    : make_idesc_f16<kB>(kTile, D, false, true);
       const uint32_t sK = smem_u32(smem + Cfg::kOffK);
       const uint32_t sV = smem_u32(smem + Cfg::kOffV);
       const uint32_t sS = smem_u32(smem + Cfg::kOffS);
@@ -427,13 +501,16 @@ __global__ void __launch_bounds__(MainCfg<D>::kThreads, 1)
       const uint32_t t_dV = tmem + Cfg::kColdV;
       const uint32_t t_dK = tmem + Cfg::kColdK;
       const uint32_t t_dQ = tmem + Cfg::kColdQ;
-      bool ok = mbar_wait(&bar[kBarKV], 0, ctx, 30);
-      for (int i = 0; i < mt && ok; ++i) {
+      // Issue order is software-pipelined by one query tile:
+      //   dP_0 dV_0 | dP_1 dV_1 dK_0 dQ_0 | dP_2 dV_2 dK_1 dQ_1 | ...
+      // so the dS epilogue of tile i overlaps dK_{i-1}, dQ_{i-1}, dP_{i+1}
+      // and dV_{i+1} on the tensor pipe.
+      auto issue_dP_dV = [&](int i) -> bool {
         const int s = i & 1;
         const uint32_t sP = smem_u32(smem + Cfg::kOffP + s * Cfg::kPT);
         // dP = dO_i V_j^T : A = dO_i (K-major over d), B = V_j (K-major over d).
-        if (!mbar_wait(&bar[kBarDOFull], i & 1, ctx, 31)) { ok = false; break; }
-        if (i > 0 && !mbar_wait(&bar[kBarDPEmpty], (i - 1) & 1, ctx, 32)) { ok = false; break; }
+        if (!mbar_wait(&bar[kBarDOFull], i & 1, ctx, 31)) return false;
+        if (i > 0 && !mbar_wait(&bar[kBarDPEmpty], (i - 1) & 1, ctx, 32)) return false;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
@@ -443,8 +520,7 @@ __global__ void __launch_bounds__(MainCfg<D>::kThreads, 1)
         }
         umma_commit(&bar[kBarDPFull]);
         // dV += P_ij^T dO_i : A = P^T (MN-major, M = key), B = dO_i (MN-major, N = d).
-        if (!mbar_wait(&bar[kBarPFull0 + s], (i >> 1) & 1, ctx, 33)) { ok = false; break; }
-        tc_fence_after();
+        if (!mbar_wait(&bar[kBarPFull0 + s], (i >> 1) & 1, ctx, 33)) return false;
 #pragma unroll
         for (int k = 0; k < kTile / 16; ++k) {
           umma_f16_ss(t_dV, make_sw128_desc(sP + k * 2048, kBoxBytes, 1024),
@@ -453,10 +529,12 @@ __global__ void __launch_bounds__(MainCfg<D>::kThreads, 1)
         }
         umma_commit(&bar[kBarDOEmpty]);
         umma_commit(&bar[kBarPEmpty0 + s]);
+        return true;
+      };
+      auto issue_dK_dQ = [&](int i) -> bool {
         // dK += dS^T Q_i : A = dS^T (MN-major, M = key), B = Q_i (MN-major, N = d).
-        if (!mbar_wait(&bar[kBarQFull], i & 1, ctx, 34)) { ok = false; break; }
-        if (!mbar_wait(&bar[kBarDSFull], i & 1, ctx, 35)) { ok = false; break; }
-        tc_fence_after();
+        if (!mbar_wait(&bar[kBarQFull], i & 1, ctx, 34)) return false;
+        if (!mbar_wait(&bar[kBarDSFull], i & 1, ctx, 35)) return false;
 #pragma unroll
         for (int k = 0; k < kTile / 16; ++k) {
           umma_f16_ss(t_dK, make_sw128_desc(sS + k * 2048, kBoxBytes, 1024),
@@ -464,29 +542,38 @@ __global__ void __launch_bounds__(MainCfg<D>::kThreads, 1)
                       (i > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(&bar[kBarQEmpty]);
-        // dQ_i = dS K_j : A = dS (K-major over keys), B = K_j (MN-major, N = d).
-        if (i > 0 && !mbar_wait(&bar[kBarDQEmpty], (i - 1) & 1, ctx, 36)) { ok = false; break; }
+        // dQ partial over this key tile (reduction over the 128 keys).
+        if (i > 0 && !mbar_wait(&bar[kBarDQEmpty], (i - 1) & 1, ctx, 36)) return false;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < kTile / 16; ++k) {
-          umma_f16_ss(t_dQ, make_sw128_desc(sS + (k >> 2) * kBoxBytes + (k & 3) * 32, 16, 1024),
-                      make_sw128_desc(sK + k * 2048, kBoxBytes, 1024), id_dQ, k > 0 ? 1u : 0u);
+          const uint64_t ds_kmajor =
+              make_sw128_desc(sS + (k >> 2) * kBoxBytes + (k & 3) * 32, 16, 1024);
+          const uint64_t k_mnmajor = make_sw128_desc(sK + k * 2048, kBoxBytes, 1024);
+          if constexpr (Cfg::kDQTransposed)
+            umma_f16_ss(t_dQ, k_mnmajor, ds_kmajor, id_dQ, k > 0 ? 1u : 0u);
+          else
+            umma_f16_ss(t_dQ, ds_kmajor, k_mnmajor, id_dQ, k > 0 ? 1u : 0u);
         }
         umma_commit(&bar[kBarDQFull]);
         umma_commit(&bar[kBarDSEmpty]);
-      }
+        return true;
+      };
+      const bool is_a = (warp == 1);
+      bool ok = mbar_wait(&bar[kBarKV], 0, ctx, 30);
+      for (int i = 0; i < mt && ok; ++i) ok = is_a ? issue_dP_dV(i) : issue_dK_dQ(i);
+      uint64_t* drain = &bar[is_a ? kBarDrain : kBarDrain2];
       if (ok) {
         umma_commit(&bar[kBarAccFull]);
       } else {
-        umma_commit(&bar[kBarDrain]);
-        mbar_wait_drain(&bar[kBarDrain], 0, timeout_ns);
+        umma_commit(drain);
+        mbar_wait_drain(drain, 0, timeout_ns);
       }
     }
-  } else {
-    // ---- Epilogue: 8 warps. Warp w owns TMEM lane quarter q = w % 4 (rows
-    // 32q..32q+31 of the tile) and column half c.
+  } else if (warp >= Cfg::kFirstDSWarp && warp < Cfg::kFirstDQWarp) {
+    // ---- dS warps.
     const int q = warp & 3;
-    const int c = (warp - 3) >> 2;
+    const int c = (warp - Cfg::kFirstDSWarp) >> 2;
     const int r = q * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const uint32_t rsw = static_cast<uint32_t>(r);
@@ -495,67 +582,44 @@ __global__ void __launch_bounds__(MainCfg<D>::kThreads, 1)
       const int s = i & 1;
       const int m = i * kTile + r;
       const float Dm = (m < M) ? __ldg(Dsum + static_cast<int64_t>(h) * M + m) : 0.f;
-      // (a) dP row segment -> registers
       if (!mbar_wait(&bar[kBarDPFull], i & 1, ctx, 40)) { ok = false; break; }
+      __syncwarp();
       tc_fence_after();
-      uint32_t dp[64];
-      tmem_ld_32x32b_x32(lane_base + Cfg::kColdP + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
-      tmem_ld_32x32b_x32(lane_base + Cfg::kColdP + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[32]));
-      tmem_ld_wait();
+      // Both 32-column halves of this warp's dP segment are loaded before any
+      // other work, then the TMEM is released.
+      uint32_t dpa[32], dpb[32];
+      tmem_load_32(lane_base + Cfg::kColdP + c * 64, dpa);
+      tmem_load_32(lane_base + Cfg::kColdP + c * 64 + 32, dpb);
+      if (!mbar_wait(&bar[kBarPFull0 + s], (i >> 1) & 1, ctx, 41)) { ok = false; break; }
+      __syncwarp();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kBarDPEmpty]);
-      // (b) dS = P * (dP - D) for columns 64c..64c+63 (= box c of the P tile)
-      if (!mbar_wait(&bar[kBarPFull0 + s], (i >> 1) & 1, ctx, 41)) { ok = false; break; }
       const uint8_t* pbox = smem + Cfg::kOffP + s * Cfg::kPT + c * kBoxBytes;
-      uint32_t ds[32];
+      uint4 ds[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         const uint4 pv = *reinterpret_cast<const uint4*>(pbox + sw128_offset(rsw, j));
-        const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
+        ds[j] = ds_chunk<T>(pv, dpa + 8 * j, Dm);
+      }
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float2 p = Elem<T>::unpack(pw[t]);
-          const float a = p.x * (__uint_as_float(dp[j * 8 + 2 * t]) - Dm);
-          const float b = p.y * (__uint_as_float(dp[j * 8 + 2 * t + 1]) - Dm);
-          ds[j * 4 + t] = Elem<T>::pack(a, b);
-        }
+      for (int j = 0; j < 4; ++j) {
+        const uint4 pv = *reinterpret_cast<const uint4*>(pbox + sw128_offset(rsw, 4 + j));
+        ds[4 + j] = ds_chunk<T>(pv, dpb + 8 * j, Dm);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kBarPEmpty0 + s]);
       if (i > 0 && !mbar_wait(&bar[kBarDSEmpty], (i - 1) & 1, ctx, 42)) { ok = false; break; }
       uint8_t* sbox = smem + Cfg::kOffS + c * kBoxBytes;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        *reinterpret_cast<uint4*>(sbox + sw128_offset(rsw, j)) =
-            make_uint4(ds[j * 4 + 0], ds[j * 4 + 1], ds[j * 4 + 2], ds[j * 4 + 3]);
-      }
+      for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(sbox + sw128_offset(rsw, j)) = ds[j];
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kBarDSFull]);
-      // (c) dQ_i partial -> fp32 accumulator
-      if (!mbar_wait(&bar[kBarDQFull], i & 1, ctx, 43)) { ok = false; break; }
-      tc_fence_after();
-      constexpr int kHalf = D / 2;  // dQ columns per warp
-      uint32_t dq[kHalf];
-#pragma unroll
-      for (int x = 0; x < kHalf / 32; ++x)
-        tmem_ld_32x32b_x32(lane_base + Cfg::kColdQ + c * kHalf + x * 32,
-                           *reinterpret_cast<uint32_t(*)[32]>(&dq[x * 32]));
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kBarDQEmpty]);
-      if (m < M) {
-        float* dst = dQacc + (static_cast<int64_t>(h) * M + m) * D + c * kHalf;
-#pragma unroll
-        for (int x = 0; x < kHalf / 4; ++x)
-          red_add_v4_f32(dst + 4 * x, __uint_as_float(dq[4 * x]), __uint_as_float(dq[4 * x + 1]),
-                         __uint_as_float(dq[4 * x + 2]), __uint_as_float(dq[4 * x + 3]));
-      }
     }
-    // (d) final dV_j and dK_j rows (lane = key row) -> 16-bit outputs
+    // final dV_j and dK_j rows (lane = key row) -> 16-bit outputs
     if (ok && mbar_wait(&bar[kBarAccFull], 0, ctx, 44)) {
+      __syncwarp();
       tc_fence_after();
       const int n = n0 + r;
       constexpr int kHalf = D / 2;
@@ -566,8 +630,7 @@ __global__ void __launch_bounds__(MainCfg<D>::kThreads, 1)
 #pragma unroll
         for (int x = 0; x < kHalf / 32; ++x) {
           uint32_t v[32];
-          tmem_ld_32x32b_x32(lane_base + col + x * 32, v);
-          tmem_ld_wait();
+          tmem_load_32(lane_base + col + x * 32, v);
           if (n < N) {
             uint4* o = reinterpret_cast<uint4*>(out + x * 32);
 #pragma unroll
@@ -581,6 +644,46 @@ __global__ void __launch_bounds__(MainCfg<D>::kThreads, 1)
         }
       }
       tc_fence_before();
+    }
+  } else if (warp >= Cfg::kFirstDQWarp) {
+    // ---- dQ warps: TMEM -> registers -> fp32 accumulator.
+    const int q = warp & 3;
+    const int c = (warp - Cfg::kFirstDQWarp) >> 2;
+    constexpr int kCols = Cfg::kdQCols / 2;  // columns of the dQ partial per warp
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + Cfg::kColdQ + c * kCols;
+    for (int i = 0; i < mt; ++i) {
+      if (!mbar_wait(&bar[kBarDQFull], i & 1, ctx, 50)) break;
+      __syncwarp();
+      tc_fence_after();
+      uint32_t v[kCols];
+      if constexpr (kCols == 64)
+        tmem_load_64(lane_base, *reinterpret_cast<uint32_t(*)[64]>(&v[0]));
+      else
+        tmem_load_32(lane_base, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kBarDQEmpty]);
+      const int mbase = i * kTile;
+      if constexpr (Cfg::kDQTransposed) {
+        // lane = d (32q + lane), column = query row mbase + c*64 + j: one
+        // 128-byte line of a dQ row per warp-wide reduction.
+        const int m0 = mbase + c * kCols;
+        const int valid = min(kCols, M - m0);
+        float* p = dQacc + (static_cast<int64_t>(h) * M + m0) * D + q * 32 + lane;
+#pragma unroll
+        for (int j = 0; j < kCols; ++j)
+          if (j < valid) red_add_f32(p + static_cast<int64_t>(j) * D, __uint_as_float(v[j]));
+      } else {
+        // lane = query row (32q + lane), column = d (c*32 .. c*32+31).
+        const int m = mbase + q * 32 + lane;
+        if (m < M) {
+          float* dst = dQacc + (static_cast<int64_t>(h) * M + m) * D + c * kCols;
+#pragma unroll
+          for (int y = 0; y < kCols / 4; ++y)
+            red_add_v4_f32(dst + 4 * y, __uint_as_float(v[4 * y]), __uint_as_float(v[4 * y + 1]),
+                           __uint_as_float(v[4 * y + 2]), __uint_as_float(v[4 * y + 3]));
+        }
+      }
     }
   }
 
