@@ -26,7 +26,9 @@ FMHA_API int fmha_bwd_poll_device_status(void) {
   auto it = m.find(device);
   if (it == m.end() || it->second.host_status == nullptr) return fmha_sm100::kOk;
   const fmha_sm100::KernelStatus st = fmha_sm100::read_status(it->second.host_status);
-  return st.code != 0 ? fmha_sm100::kErrDeviceTimeout : fmha_sm100::kOk;
+  if (st.code == 0) return fmha_sm100::kOk;
+  memset(it->second.host_status, 0, sizeof(fmha_sm100::KernelStatus));
+  return fmha_sm100::kErrDeviceTimeout;
 }
 
 FMHA_API void fmha_bwd_set_wait_timeout_ms(int ms) {

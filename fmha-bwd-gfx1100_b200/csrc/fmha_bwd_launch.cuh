@@ -5,9 +5,9 @@
 //
 // Replaces the body of fmha_bwd_full_py (src/fmha_bwd_kernels.hip:475-523)
 // and fmha_bwd_full_fp16 (src/fmha_bwd_kernels_fp16.hip:236-280):
-//   * no per-call dP/dS allocation (those never leave the SM); the workspace
-//     is H*M fp32 rowsums + H*M*d fp32 dQ accumulator, cached per device and
-//     grown on demand;
+//   * no per-call dP/dS allocation (those never leave the SM); the only
+//     workspace is the H*M fp32 rowsum D, cached per device and grown on
+//     demand;
 //   * shapes and pointers are checked before anything is launched, so a bad
 //     call leaves the outputs untouched and reports an error code;
 //   * 64-bit offsets throughout.
@@ -108,11 +108,8 @@ inline bool encode_map(CUtensorMap* map, bool bf16, const void* base, uint64_t c
 struct DeviceWorkspace {
   float* dsum = nullptr;
   size_t dsum_floats = 0;
-  float* dqacc = nullptr;
-  size_t dqacc_floats = 0;
-  KernelStatus* status = nullptr;       // device memory
-  KernelStatus* host_status = nullptr;  // mapped pinned host memory
-  KernelStatus* host_status_dev = nullptr;
+  KernelStatus* host_status = nullptr;      // mapped pinned host memory
+  KernelStatus* host_status_dev = nullptr;  // its device address
   bool attrs_set = false;
   int sm_count = 0;
 };
@@ -153,28 +150,23 @@ inline uint64_t effective_timeout_ns() {
 
 template <typename T>
 void set_kernel_attrs() {
-  cudaFuncSetAttribute(rowsum_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       RowsumCfg<64>::kSmemBytes);
-  cudaFuncSetAttribute(rowsum_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       RowsumCfg<128>::kSmemBytes);
-  cudaFuncSetAttribute(main_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       MainCfg<64>::kSmemBytes);
-  cudaFuncSetAttribute(main_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       MainCfg<128>::kSmemBytes);
+  cudaFuncSetAttribute(dq_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       DqCfg<64>::kSmemBytes);
+  cudaFuncSetAttribute(dq_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       DqCfg<128>::kSmemBytes);
+  cudaFuncSetAttribute(dkv_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       DkvCfg<64>::kSmemBytes);
+  cudaFuncSetAttribute(dkv_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       DkvCfg<128>::kSmemBytes);
 }
 
 // Returns the workspace of the current device with at least the requested
 // capacity, or nullptr (error already recorded).
 template <typename T>
-DeviceWorkspace* get_workspace(int device, size_t dsum_floats, size_t dqacc_floats) {
+DeviceWorkspace* get_workspace(int device, size_t dsum_floats) {
   std::lock_guard<std::mutex> g(ws_mutex());
   DeviceWorkspace& w = ws_map()[device];
-  if (!w.status) {
-    if (cudaMalloc(&w.status, sizeof(KernelStatus)) != cudaSuccess) {
-      set_error(kErrOutOfMemory, "status word allocation failed");
-      return nullptr;
-    }
-    cudaMemset(w.status, 0, sizeof(KernelStatus));
+  if (!w.host_status) {
     if (cudaHostAlloc(&w.host_status, sizeof(KernelStatus),
                       cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess ||
         cudaHostGetDevicePointer(&w.host_status_dev, w.host_status, 0) != cudaSuccess) {
@@ -199,18 +191,6 @@ DeviceWorkspace* get_workspace(int device, size_t dsum_floats, size_t dqacc_floa
       return nullptr;
     }
     w.dsum_floats = dsum_floats;
-  }
-  if (dqacc_floats > w.dqacc_floats) {
-    if (w.dqacc) cudaFree(w.dqacc);
-    w.dqacc = nullptr;
-    w.dqacc_floats = 0;
-    if (cudaMalloc(&w.dqacc, dqacc_floats * sizeof(float)) != cudaSuccess) {
-      cudaGetLastError();
-      set_error(kErrOutOfMemory, "workspace allocation of %zu bytes failed",
-                dqacc_floats * sizeof(float));
-      return nullptr;
-    }
-    w.dqacc_floats = dqacc_floats;
   }
   return &w;
 }
@@ -248,7 +228,7 @@ inline int check_args(const void* dQ, const void* dK, const void* dV, const void
   return kOk;
 }
 
-// Launches the three kernels on `stream`. When `sync` is set, waits for the
+// Launches the two kernels on `stream`. When `sync` is set, waits for the
 // stream and reports in-kernel wait timeouts as kErrDeviceTimeout.
 template <typename T>
 int run_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const T* P,
@@ -268,7 +248,7 @@ int run_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const 
     return set_error(kErrUnsupportedDevice, "device %d is sm_%d%d; this library needs sm_100", device,
                      major, minor);
   const size_t rows = static_cast<size_t>(H) * static_cast<size_t>(M);
-  DeviceWorkspace* w = get_workspace<T>(device, rows, rows * static_cast<size_t>(D));
+  DeviceWorkspace* w = get_workspace<T>(device, rows);
   if (!w) return kErrOutOfMemory;
 
   constexpr bool kBF16 = Elem<T>::kBF16;
@@ -280,46 +260,41 @@ int run_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const 
     return set_error(kErrInvalidArgument, "tensor map encoding failed (M=%d N=%d K_dim=%d heads=%d)",
                      M, N, D, H);
 
+  if (sync) memset(w->host_status, 0, sizeof(KernelStatus));
   const uint64_t tmo = effective_timeout_ns();
-  // Optional timing events at the kernel boundaries: [0] before the rowsum
-  // kernel, [1] before the main kernel, [2] before dQ finalize, [3] after it.
+  // Optional timing events at the kernel boundaries: [0] before dq_kernel,
+  // [1] between the two kernels, [2] and [3] after dkv_kernel.
   auto mark = [&](int k) {
     if (events && events[k]) cudaEventRecord(events[k], stream);
   };
-  mark(0);
   const dim3 grid_rows((M + kTile - 1) / kTile, H);
   const dim3 grid_cols((N + kTile - 1) / kTile, H);
+  KernelStatus* st = w->host_status_dev;
+  mark(0);
   if (D == 128) {
-    rowsum_kernel<T, 128><<<grid_rows, RowsumCfg<128>::kThreads, RowsumCfg<128>::kSmemBytes, stream>>>(
-        mP, mV, dO, w->dsum, w->dqacc, M, N, w->status, tmo);
+    dq_kernel<T, 128><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
+        mP, mV, mK, mdO, dQ, w->dsum, M, N, st, tmo);
     mark(1);
-    main_kernel<T, 128><<<grid_cols, MainCfg<128>::kThreads, MainCfg<128>::kSmemBytes, stream>>>(
-        mQ, mK, mV, mdO, mP, w->dsum, w->dqacc, dK, dV, M, N, w->status, tmo);
+    dkv_kernel<T, 128><<<grid_cols, DkvCfg<128>::kThreads, DkvCfg<128>::kSmemBytes, stream>>>(
+        mQ, mV, mdO, mP, w->dsum, dK, dV, M, N, st, tmo);
   } else {
-    rowsum_kernel<T, 64><<<grid_rows, RowsumCfg<64>::kThreads, RowsumCfg<64>::kSmemBytes, stream>>>(
-        mP, mV, dO, w->dsum, w->dqacc, M, N, w->status, tmo);
+    dq_kernel<T, 64><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
+        mP, mV, mK, mdO, dQ, w->dsum, M, N, st, tmo);
     mark(1);
-    main_kernel<T, 64><<<grid_cols, MainCfg<64>::kThreads, MainCfg<64>::kSmemBytes, stream>>>(
-        mQ, mK, mV, mdO, mP, w->dsum, w->dqacc, dK, dV, M, N, w->status, tmo);
+    dkv_kernel<T, 64><<<grid_cols, DkvCfg<64>::kThreads, DkvCfg<64>::kSmemBytes, stream>>>(
+        mQ, mV, mdO, mP, w->dsum, dK, dV, M, N, st, tmo);
   }
-  const int64_t count = static_cast<int64_t>(rows) * D;
-  int64_t blocks = (count / 8 + 255) / 256;
-  const int64_t cap = static_cast<int64_t>(w->sm_count > 0 ? w->sm_count : 148) * 8;
-  if (blocks > cap) blocks = cap;
-  if (blocks < 1) blocks = 1;
   mark(2);
-  dq_finalize_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-      w->dqacc, dQ, count, w->status, w->host_status_dev);
   mark(3);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(kErrLaunch, "launch failed: %s", cudaGetErrorString(e));
   if (sync) {
     e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess) return set_error(kErrLaunch, "kernel failed: %s", cudaGetErrorString(e));
-    const KernelStatus st = read_status(w->host_status);
-    if (st.code != 0)
+    const KernelStatus stv = read_status(w->host_status);
+    if (stv.code != 0)
       return set_error(kErrDeviceTimeout, "in-kernel wait gave up (code %d, site %d, block %d)",
-                       st.code, st.where, st.block);
+                       stv.code, stv.where, stv.block);
   }
   return set_error(kOk, "");
 }
