@@ -1,5 +1,5 @@
 // Host side of the attention-backward C-ABI: argument checks, per-device
-// workspace, TMA tensor maps and the three launches. Included once by each
+// workspace, TMA tensor maps and the two launches. Included once by each
 // library translation unit (bf16 and fp16), which instantiates it for its
 // element type and defines the extern "C" entry points.
 //

@@ -72,9 +72,10 @@ int fmha_bwd_full_stream(fmha_bf16_t* dQ, fmha_bf16_t* dK, fmha_bf16_t* dV,
                          int total_heads, fmha_stream_t stream);
 
 /* Profiling variant of fmha_bwd_full_stream: additionally records the four
- * CUDA events in `events` (cudaEvent_t[4], entries may be NULL) on `stream`
- * before the rowsum kernel, before the main kernel, before the dQ finalize
- * kernel and after it, so a caller can time each kernel inside a run.
+ * CUDA events in `events` (cudaEvent_t[4], entries may be NULL) on `stream`:
+ * [0] before the query-major dQ kernel, [1] between it and the key-major
+ * dK/dV kernel, [2] and [3] after the dK/dV kernel, so a caller can time each
+ * kernel inside a run.
  * No counterpart in the reference. */
 int fmha_bwd_full_stream_events(fmha_bf16_t* dQ, fmha_bf16_t* dK,
                                 fmha_bf16_t* dV, const fmha_bf16_t* Q,
@@ -120,8 +121,9 @@ int fmha_bwd_last_error(void);
 /* Human-readable message for the most recent error ("" if none). */
 const char* fmha_bwd_last_error_message(void);
 
-/* Reads the device status word written by the most recently completed call
- * on the current device: 0 if every in-kernel wait completed, else
+/* Reads and clears the status slot of the current device (host-mapped
+ * memory that the kernels write when an in-kernel wait runs out): 0 if every
+ * wait of every call since the last poll completed, else
  * FMHA_BWD_ERR_DEVICE_TIMEOUT. Call after synchronising the stream. */
 int fmha_bwd_poll_device_status(void);
 
