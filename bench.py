@@ -225,8 +225,9 @@ def main() -> int:
     ap.add_argument("--workload", default="flux")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-rows", type=int, default=512,
-                    help="query rows per head in the CPU baseline sample")
+    ap.add_argument("--cpu-rows", type=int, default=0,
+                    help="query rows per head in the CPU baseline sample (0: all M rows, "
+                         "i.e. whole heads, about 10-15 s on 16 host cores at FLUX)")
     ap.add_argument("--cpu-rows-per-step", type=int, default=0,
                     help="query rows per head per step of the reference arm "
                          "(0: sized so the run takes about two minutes)")
@@ -325,11 +326,8 @@ def main() -> int:
     # ---- gather timings and checksums (NCCL, after the timed region)
     checksum = float(dQ.float().sum().item() + dK.float().sum().item() + dV.float().sum().item())
     if world > 1:
-        t = torch.tensor([ms_total, statistics.mean(t_dkv), checksum], device=dev,
-                         dtype=torch.float64)
-        allt = [torch.zeros_like(t) for _ in range(world)]
-        dist.all_gather(allt, t)
-        allt = torch.stack(allt).cpu()
+        allt = workloads.gather_rank_stats(dist, [ms_total, statistics.mean(t_dkv), checksum],
+                                           dev)
         ms_max = float(allt[:, 0].max())
         main_ms = float(allt[:, 1].max())
         checksums = [float(x) for x in allt[:, 2]]
@@ -428,11 +426,13 @@ def main() -> int:
     }
     if world == 1 and not args.no_cpu_baseline:
         threads = cpu_threads(w)
-        fl, dt, kind, cores = cpu_reference_sample(w, args.cpu_rows, threads)
+        rows = args.cpu_rows if args.cpu_rows > 0 else w.M
+        fl, dt, kind, cores = cpu_reference_sample(w, rows, threads)
         line["cpu_baseline"] = {
             "value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": kind,
-            "sample": f"first {args.cpu_rows} of {w.M} query rows x {w.N} keys x d={w.d} for "
-                      f"{threads} heads, one head per thread, {dt:.1f} s",
+            "sample": f"{rows} of {w.M} query rows x {w.N} keys x d={w.d} for {threads} of "
+                      f"{w.heads} heads, one head per thread (reference fmha_backward_cpu), "
+                      f"{dt:.1f} s",
         }
     print(json.dumps(line), flush=True)
     return 0

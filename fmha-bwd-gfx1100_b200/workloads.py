@@ -96,3 +96,14 @@ def head_range(total_heads: int, rank: int, world: int) -> tuple[int, int]:
     h0 = min(total_heads, rank * per)
     h1 = min(total_heads, h0 + per)
     return h0, h1
+
+
+def gather_rank_stats(dist, values, device) -> torch.Tensor:
+    """All-gather one row of float64 statistics per rank (timings, checksums)
+    after the timed region; returns a [world, len(values)] CPU tensor. Every
+    rank must call it with the same number of values. With the NCCL backend
+    ``device`` is the rank's GPU; with gloo it is the CPU."""
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    parts = [torch.zeros_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(parts, t)
+    return torch.stack(parts).cpu()
