@@ -7,6 +7,53 @@
 
 using bf16 = __nv_bfloat16;
 
+// ------------------------------------------------------------ no-alloc entry
+// fmha_bwd_full_noalloc runs the same two kernels with the rowsum scratch
+// (D, one float per query row and head) and the wait-status slot taken from
+// the file-scope device arrays below instead of from cudaMalloc'd /
+// cudaHostAlloc'd memory. It serves callers that must not allocate device
+// memory from inside a library call.
+namespace {
+
+// Upper bound on total_heads * M for the no-alloc entry point: 2^20 rows of
+// fp32 D, 4 MiB of device memory per device that loads this library.
+constexpr size_t kNoAllocMaxRows = size_t(1) << 20;
+
+static __device__ __align__(256) float g_noalloc_dsum[kNoAllocMaxRows];
+static __device__ __align__(256) fmha_sm100::KernelStatus g_noalloc_status;
+
+constexpr int kNoAllocMaxDevices = 64;
+
+struct NoAllocSlot {
+  float* dsum = nullptr;
+  fmha_sm100::KernelStatus* status = nullptr;
+  int rc = 0;  // cudaError_t of the set-up
+};
+
+NoAllocSlot g_noalloc_slots[kNoAllocMaxDevices];
+std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+
+// Once per device, with that device current: device addresses of the two
+// scratch arrays, and the kernels' shared-memory attributes.
+const NoAllocSlot& noalloc_setup(int device) {
+  std::call_once(g_noalloc_once[device], [device] {
+    NoAllocSlot& s = g_noalloc_slots[device];
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.dsum), g_noalloc_dsum);
+    if (e == cudaSuccess)
+      e = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.status), g_noalloc_status);
+    if (e == cudaSuccess) {
+      fmha_sm100::set_kernel_attrs<bf16>();
+      e = cudaGetLastError();
+    } else {
+      cudaGetLastError();
+    }
+    s.rc = static_cast<int>(e);
+  });
+  return g_noalloc_slots[device];
+}
+
+}  // namespace
+
 extern "C" {
 
 FMHA_API void fmha_bwd_full_py(bf16* dQ, bf16* dK, bf16* dV, const bf16* Q, const bf16* K, const bf16* V,
@@ -27,6 +74,83 @@ FMHA_API int fmha_bwd_full_stream_events(bf16* dQ, bf16* dK, bf16* dV, const bf1
                              int total_heads, cudaStream_t stream, cudaEvent_t const* events) {
   return fmha_sm100::run_backward<bf16>(dQ, dK, dV, Q, K, V, P, dO, M, N, K_dim, total_heads,
                                         stream, /*sync=*/false, events);
+}
+
+// No counterpart in the reference. Same operation and preconditions as
+// fmha_bwd_full_stream, plus total_heads * M <= kNoAllocMaxRows; allocates
+// nothing. Enqueues on `stream`, waits for it, and returns 0 or an error code.
+// The first call on a device looks up the scratch arrays' addresses (module
+// load included); that first call should come before any stream capture.
+// Every call shares the one scratch: calls that overlap on the GPU (other
+// streams, other host threads) race.
+FMHA_API int fmha_bwd_full_noalloc(bf16* dQ, bf16* dK, bf16* dV, const bf16* Q, const bf16* K,
+                                   const bf16* V, const bf16* P, const bf16* dO, int M, int N,
+                                   int K_dim, int total_heads, cudaStream_t stream) {
+  using namespace fmha_sm100;
+  int rc = check_args(dQ, dK, dV, Q, K, V, P, dO, M, N, K_dim, total_heads);
+  if (rc != kOk) return rc;
+  const size_t rows = static_cast<size_t>(total_heads) * static_cast<size_t>(M);
+  if (rows > kNoAllocMaxRows)
+    return set_error(kErrInvalidArgument,
+                     "total_heads*M = %zu exceeds the no-alloc scratch limit of %zu rows", rows,
+                     kNoAllocMaxRows);
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(kErrLaunch, "no current CUDA device");
+  }
+  if (device < 0 || device >= kNoAllocMaxDevices)
+    return set_error(kErrInvalidArgument, "device ordinal %d beyond %d", device, kNoAllocMaxDevices);
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (major != 10 || minor != 0)
+    return set_error(kErrUnsupportedDevice, "device %d is sm_%d%d; this library needs sm_100", device,
+                     major, minor);
+  const NoAllocSlot& slot = noalloc_setup(device);
+  if (slot.rc != 0)
+    return set_error(kErrLaunch, "no-alloc scratch set-up failed: %s",
+                     cudaGetErrorString(static_cast<cudaError_t>(slot.rc)));
+
+  CUtensorMap mQ, mK, mV, mdO, mP;
+  if (!encode_fn()) return set_error(kErrNoDriver, "cuTensorMapEncodeTiled is unavailable");
+  if (!encode_map(&mQ, true, Q, K_dim, M, total_heads) ||
+      !encode_map(&mK, true, K, K_dim, N, total_heads) ||
+      !encode_map(&mV, true, V, K_dim, N, total_heads) ||
+      !encode_map(&mdO, true, dO, K_dim, M, total_heads) ||
+      !encode_map(&mP, true, P, N, M, total_heads))
+    return set_error(kErrInvalidArgument, "tensor map encoding failed (M=%d N=%d K_dim=%d heads=%d)",
+                     M, N, K_dim, total_heads);
+
+  // The status slot must start at zero; D needs no clearing (dq_kernel
+  // writes every row that dkv_kernel reads, earlier on the same stream).
+  cudaError_t e = cudaMemsetAsync(slot.status, 0, sizeof(KernelStatus), stream);
+  if (e != cudaSuccess) return set_error(kErrLaunch, "status reset failed: %s", cudaGetErrorString(e));
+  const uint64_t tmo = effective_timeout_ns();
+  const dim3 grid_rows((M + kTile - 1) / kTile, total_heads);
+  const dim3 grid_cols((N + kTile - 1) / kTile, total_heads);
+  if (K_dim == 128) {
+    dq_kernel<bf16, 128><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
+        mP, mV, mK, mdO, dQ, slot.dsum, M, N, slot.status, tmo);
+    dkv_kernel<bf16, 128><<<grid_cols, DkvCfg<128>::kThreads, DkvCfg<128>::kSmemBytes, stream>>>(
+        mQ, mV, mdO, mP, slot.dsum, dK, dV, M, N, slot.status, tmo);
+  } else {
+    dq_kernel<bf16, 64><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
+        mP, mV, mK, mdO, dQ, slot.dsum, M, N, slot.status, tmo);
+    dkv_kernel<bf16, 64><<<grid_cols, DkvCfg<64>::kThreads, DkvCfg<64>::kSmemBytes, stream>>>(
+        mQ, mV, mdO, mP, slot.dsum, dK, dV, M, N, slot.status, tmo);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(kErrLaunch, "launch failed: %s", cudaGetErrorString(e));
+  e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return set_error(kErrLaunch, "kernel failed: %s", cudaGetErrorString(e));
+  KernelStatus st{};
+  e = cudaMemcpy(&st, slot.status, sizeof(KernelStatus), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return set_error(kErrLaunch, "status read failed: %s", cudaGetErrorString(e));
+  if (st.code != 0)
+    return set_error(kErrDeviceTimeout, "in-kernel wait gave up (code %d, site %d, block %d)",
+                     st.code, st.where, st.block);
+  return set_error(kOk, "");
 }
 
 }  // extern "C"

@@ -84,6 +84,23 @@ int fmha_bwd_full_stream_events(fmha_bf16_t* dQ, fmha_bf16_t* dK,
                                 int M, int N, int K_dim, int total_heads,
                                 fmha_stream_t stream, void* const* events);
 
+/* No counterpart in the reference. Allocation-free variant of
+ * fmha_bwd_full_stream: the fp32 rowsum scratch D (total_heads * M floats)
+ * and the wait-status slot live in file-scope __device__ arrays of the
+ * library instead of cudaMalloc / cudaHostAlloc memory, so the call makes no
+ * allocation of any kind. Limit: total_heads * M <= 1048576 (4 MiB of
+ * scratch); larger calls return FMHA_BWD_ERR_INVALID_ARGUMENT before any
+ * launch. Enqueues on `stream`, waits for that stream and returns 0 or an
+ * error code (in-kernel wait timeouts included). The first call on a device
+ * looks up the scratch addresses (cudaGetSymbolAddress, which loads the
+ * module); make that first call before any stream capture. All calls share
+ * the one scratch: calls that overlap on the GPU race. */
+int fmha_bwd_full_noalloc(fmha_bf16_t* dQ, fmha_bf16_t* dK, fmha_bf16_t* dV,
+                          const fmha_bf16_t* Q, const fmha_bf16_t* K,
+                          const fmha_bf16_t* V, const fmha_bf16_t* P,
+                          const fmha_bf16_t* dO, int M, int N, int K_dim,
+                          int total_heads, fmha_stream_t stream);
+
 /* ---- libfmha_bwd_fp16.so ------------------------------------------------ */
 
 /* Replaces fmha_bwd_full_fp16, src/fmha_bwd_kernels_fp16.hip:236-238. */
