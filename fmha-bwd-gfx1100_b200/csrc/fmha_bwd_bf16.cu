@@ -112,36 +112,13 @@ FMHA_API int fmha_bwd_full_noalloc(bf16* dQ, bf16* dK, bf16* dV, const bf16* Q, 
     return set_error(kErrLaunch, "no-alloc scratch set-up failed: %s",
                      cudaGetErrorString(static_cast<cudaError_t>(slot.rc)));
 
-  CUtensorMap mQ, mK, mV, mdO, mP;
-  if (!encode_fn()) return set_error(kErrNoDriver, "cuTensorMapEncodeTiled is unavailable");
-  if (!encode_map(&mQ, true, Q, K_dim, M, total_heads) ||
-      !encode_map(&mK, true, K, K_dim, N, total_heads) ||
-      !encode_map(&mV, true, V, K_dim, N, total_heads) ||
-      !encode_map(&mdO, true, dO, K_dim, M, total_heads) ||
-      !encode_map(&mP, true, P, N, M, total_heads))
-    return set_error(kErrInvalidArgument, "tensor map encoding failed (M=%d N=%d K_dim=%d heads=%d)",
-                     M, N, K_dim, total_heads);
-
-  // The status slot must start at zero; D needs no clearing (dq_kernel
-  // writes every row that dkv_kernel reads, earlier on the same stream).
+  // The status slot must start at zero; D needs no clearing (the dQ kernel
+  // writes every row that the dK/dV kernel reads, earlier on the same stream).
   cudaError_t e = cudaMemsetAsync(slot.status, 0, sizeof(KernelStatus), stream);
   if (e != cudaSuccess) return set_error(kErrLaunch, "status reset failed: %s", cudaGetErrorString(e));
-  const uint64_t tmo = effective_timeout_ns();
-  const dim3 grid_rows((M + kTile - 1) / kTile, total_heads);
-  const dim3 grid_cols((N + kTile - 1) / kTile, total_heads);
-  if (K_dim == 128) {
-    dq_kernel<bf16, 128><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
-        mP, mV, mK, mdO, dQ, slot.dsum, M, N, slot.status, tmo);
-    dkv_kernel<bf16, 128><<<grid_cols, DkvCfg<128>::kThreads, DkvCfg<128>::kSmemBytes, stream>>>(
-        mQ, mV, mdO, mP, slot.dsum, dK, dV, M, N, slot.status, tmo);
-  } else {
-    dq_kernel<bf16, 64><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
-        mP, mV, mK, mdO, dQ, slot.dsum, M, N, slot.status, tmo);
-    dkv_kernel<bf16, 64><<<grid_cols, DkvCfg<64>::kThreads, DkvCfg<64>::kSmemBytes, stream>>>(
-        mQ, mV, mdO, mP, slot.dsum, dK, dV, M, N, slot.status, tmo);
-  }
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return set_error(kErrLaunch, "launch failed: %s", cudaGetErrorString(e));
+  rc = enqueue_backward<bf16>(dQ, dK, dV, Q, K, V, P, dO, M, N, K_dim, total_heads, slot.dsum,
+                              slot.status, stream, nullptr);
+  if (rc != kOk) return rc;
   e = cudaStreamSynchronize(stream);
   if (e != cudaSuccess) return set_error(kErrLaunch, "kernel failed: %s", cudaGetErrorString(e));
   KernelStatus st{};

@@ -31,6 +31,34 @@ FMHA_API int fmha_bwd_poll_device_status(void) {
   return fmha_sm100::kErrDeviceTimeout;
 }
 
+FMHA_API int fmha_bwd_selftest_wait_timeout(int timeout_ms) {
+  using namespace fmha_sm100;
+  if (timeout_ms <= 0 || timeout_ms > 10000)
+    return set_error(kErrInvalidArgument, "timeout_ms=%d outside (0, 10000]", timeout_ms);
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(kErrLaunch, "no current CUDA device");
+  }
+  DeviceWorkspace* w = nullptr;
+  {
+    std::lock_guard<std::mutex> g(ws_mutex());
+    w = &ws_map()[device];
+    if (!ensure_status_slot(device, *w)) return kErrOutOfMemory;
+  }
+  memset(w->host_status, 0, sizeof(KernelStatus));
+  wait_selftest_kernel<<<1, 32>>>(w->host_status_dev, static_cast<uint64_t>(timeout_ms) * 1000000ull);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return set_error(kErrLaunch, "self-test kernel failed: %s", cudaGetErrorString(e));
+  const KernelStatus st = read_status(w->host_status);
+  memset(w->host_status, 0, sizeof(KernelStatus));
+  if (st.code != kStatusWaitTimeout || st.where != kSelfTestSite)
+    return set_error(kErrLaunch, "self-test: expected a recorded wait timeout, got code %d site %d",
+                     st.code, st.where);
+  return set_error(kOk, "");
+}
+
 FMHA_API void fmha_bwd_set_wait_timeout_ms(int ms) {
   fmha_sm100::timeout_override_ns().store(ms > 0 ? static_cast<uint64_t>(ms) * 1000000ull : 0ull);
 }

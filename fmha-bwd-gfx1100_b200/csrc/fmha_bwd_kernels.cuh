@@ -33,10 +33,15 @@
 // the UMMA descriptor, which is how P^T, dS^T, Q, dO and K are consumed
 // without any explicit transpose.
 //
-// The tensor pipe keeps no queue beyond the instruction in flight, so each
-// kernel has a single issuing thread whose waits all have at least one
-// group of MMAs of slack, and every hand-off between warps goes through an
-// mbarrier (bounded waits, see sm100_ptx.cuh).
+// The tensor pipe accepts only about one MMA ahead of the one executing, so
+// any wait (even on a barrier that has already completed) or branch in the
+// issuing thread between two MMA groups idles it. dq_kernel therefore issues
+// from two threads in different warps (dP in one, the two accumulations in
+// the other) so that one keeps the pipe fed while the other waits; every
+// hand-off between warps goes through an mbarrier (bounded waits, see
+// sm100_ptx.cuh), and the streamed operands each have their own ring of
+// shared-memory slots so that a slot is refilled as soon as its own last
+// reader is done.
 #pragma once
 
 #include <cuda.h>
@@ -122,10 +127,13 @@ __device__ __forceinline__ void store_row_32(T* out, const float* v) {
 }
 
 // ================================================================ dq_kernel
-// Shared memory: dO_i [128 x D] resident, then S stages of {P_ij [128 x 128],
-// V_j [128 x D], K_j [128 x D]}; a 1 KB exchange area for the two warps that
-// share each TMEM lane quarter (values are handed over through an mbarrier
-// per quarter, so every wait is bounded); barriers.
+// Shared memory: dO_i [128 x D] resident; three rings, one per streamed
+// operand, so that each slot is released as soon as its own last reader is
+// done: V_j (read by dP_j only), P_ij (read by B_j and by the epilogue of
+// tile j) and K_j (read by B_j and A_j). D = 128: 2 slots each (224 KB);
+// D = 64: 3 slots each. A 1 KB exchange area for the two warps that share
+// each TMEM lane quarter (values are handed over through an mbarrier per
+// quarter, so every wait is bounded); barriers.
 // TMEM (512 columns): X0 [0,128), X1 [128,256) hold dP_ij; E_ij is then
 // written over the first 32 columns of each 64-column half; A [256, 256+D),
 // B [256+D, 256+2D).
@@ -133,18 +141,22 @@ template <int D>
 struct DqCfg {
   static constexpr int kMD = (D / kBoxCols) * kBoxBytes;  // [128 x D] tile
   static constexpr int kPT = 2 * kBoxBytes;               // [128 x 128] tile
-  static constexpr int kStageBytes = kPT + 2 * kMD;
-  static constexpr int kStages = D == 128 ? 2 : 3;
+  static constexpr int kSV = D == 128 ? 2 : 3;            // V_j slots
+  static constexpr int kSK = D == 128 ? 2 : 3;            // K_j slots
+  static constexpr int kSP = D == 128 ? 2 : 3;            // P_ij slots
   static constexpr int kOffdO = 0;
-  static constexpr int kOffStage = kMD;
-  static constexpr int kOffXch = kOffStage + kStages * kStageBytes;
+  static constexpr int kOffV = kMD;
+  static constexpr int kOffK = kOffV + kSV * kMD;
+  static constexpr int kOffP = kOffK + kSK * kMD;
+  static constexpr int kOffXch = kOffP + kSP * kPT;
   static constexpr int kXchBytes = 2 * kTile * 4;  // [2 halves][128 rows] fp32
   static constexpr int kOffBar = kOffXch + kXchBytes;
-  static constexpr int kBarBytes = 256;
+  static constexpr int kBarBytes = 512;
   static constexpr int kSmemBytes = kOffBar + kBarBytes + 1024;
   static constexpr int kEpiWarps = 8;
   static constexpr int kFirstEpiWarp = 2;
-  static constexpr int kThreads = 32 * (kFirstEpiWarp + kEpiWarps);
+  static constexpr int kAbWarp = kFirstEpiWarp + kEpiWarps;  // second MMA issuer
+  static constexpr int kThreads = 32 * (kAbWarp + 1);
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kColX = 0;  // + 128 * buffer
   static constexpr uint32_t kColA = 256;
@@ -155,16 +167,22 @@ struct DqCfg {
 
 enum DqBar : int {
   kQbDO = 0,
-  kQbFull0 = 1,   // + stage (up to 3)
-  kQbEmpty0 = 4,  // + stage
-  kQbXFull0 = 7,  // + buffer (2)
-  kQbEFull0 = 9,  // + buffer
-  kQbXFree0 = 11, // + buffer
-  kQbAB = 13,
-  kQbDrain = 14,
-  kQbXch0 = 15,   // + lane quarter (4): the two warps of a quarter swap values
-  kNumDqBars = 19,
+  kQbVFull0 = 1,    // + slot (up to 3)
+  kQbVEmpty0 = 4,   // + slot
+  kQbKFull0 = 7,    // + slot
+  kQbKEmpty0 = 10,  // + slot
+  kQbPFull0 = 13,   // + slot
+  kQbPEmpty0 = 16,  // + slot: MMA commit after B_j + 8 epilogue warps
+  kQbXFull0 = 19,   // + buffer (2)
+  kQbEFull0 = 21,   // + buffer
+  kQbXFree0 = 23,   // + buffer
+  kQbAB = 25,
+  kQbDrain = 26,
+  kQbXch0 = 27,     // + lane quarter (4): the two warps of a quarter swap values
+  kQbDrain2 = 31,   // drain of the second MMA issuer
+  kNumDqBars = 32,
 };
+static_assert(kNumDqBars * 8 + 8 <= 512, "dq barrier area");
 
 template <typename T, int D>
 __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
@@ -173,7 +191,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
               T* __restrict__ dQ, float* __restrict__ Dsum, int M, int N,
               KernelStatus* status, uint64_t timeout_ns) {
   using Cfg = DqCfg<D>;
-  constexpr int S = Cfg::kStages;
+  constexpr int SV = Cfg::kSV, SK = Cfg::kSK, SP = Cfg::kSP;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -190,9 +208,17 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar[kQbDO], 1);
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&bar[kQbFull0 + s], 1);
-      mbar_init(&bar[kQbEmpty0 + s], 1 + Cfg::kEpiWarps);
+    for (int s = 0; s < SV; ++s) {
+      mbar_init(&bar[kQbVFull0 + s], 1);
+      mbar_init(&bar[kQbVEmpty0 + s], 1);
+    }
+    for (int s = 0; s < SK; ++s) {
+      mbar_init(&bar[kQbKFull0 + s], 1);
+      mbar_init(&bar[kQbKEmpty0 + s], 1);
+    }
+    for (int s = 0; s < SP; ++s) {
+      mbar_init(&bar[kQbPFull0 + s], 1);
+      mbar_init(&bar[kQbPEmpty0 + s], 1 + Cfg::kEpiWarps);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bar[kQbXFull0 + b], 1);
@@ -201,6 +227,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
     }
     mbar_init(&bar[kQbAB], 1);
     mbar_init(&bar[kQbDrain], 1);
+    mbar_init(&bar[kQbDrain2], 1);
     for (int q = 0; q < 4; ++q) mbar_init(&bar[kQbXch0 + q], 2);
     *abort_flag = 0;
     fence_mbar_init();
@@ -213,10 +240,11 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  WaitCtx ctx{abort_flag, status, timeout_ns};
+  WaitCtx ctx{abort_flag, timeout_ns};
 
   if (warp == 0) {
-    // ---- TMA producer: dO_i once, then stages of {P_ij, V_j, K_j}.
+    // ---- TMA producer: dO_i once, then V_j, P_ij, K_j in the order the
+    // tensor core needs them, each into the next slot of its own ring.
     if (lane == 0) {
       tma_prefetch_desc(&tm_P);
       tma_prefetch_desc(&tm_V);
@@ -228,46 +256,64 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 #pragma unroll
       for (int b = 0; b < D / kBoxCols; ++b)
         tma_load_3d(smem + Cfg::kOffdO + b * kBoxBytes, &tm_dO, &bar[kQbDO], b * kBoxCols, m0, h, pol_kv);
-      // Only S stages fit in shared memory, fewer than the load latency
-      // needs, so tiles are first pulled into L2 kAhead key tiles ahead; the
-      // shared-memory load that follows once a stage frees is then an L2 hit.
+      // P streams from HBM: pull it into L2 a few key tiles ahead so the
+      // shared-memory load that follows once a slot frees is an L2 hit.
       constexpr int kAhead = 4;
       auto prefetch = [&](int j) {
         tma_prefetch_l2_3d(&tm_P, j * kTile, m0, h);
         tma_prefetch_l2_3d(&tm_P, j * kTile + kBoxCols, m0, h);
-        for (int b = 0; b < D / kBoxCols; ++b) {
-          tma_prefetch_l2_3d(&tm_V, b * kBoxCols, j * kTile, h);
-          tma_prefetch_l2_3d(&tm_K, b * kBoxCols, j * kTile, h);
-        }
       };
       for (int j = 0; j < kAhead && j < nt; ++j) prefetch(j);
-      int issued = 0;
+      int nV = 0, nP = 0, nK = 0;  // loads issued per ring
       for (int j = 0; j < nt; ++j) {
-        const int s = j % S;
-        const int u = j / S;
         if (j + kAhead < nt) prefetch(j + kAhead);
-        if (u > 0 && !mbar_wait(&bar[kQbEmpty0 + s], (u - 1) & 1, ctx, 1)) break;
-        uint8_t* st = smem + Cfg::kOffStage + s * Cfg::kStageBytes;
-        uint64_t* fb = &bar[kQbFull0 + s];
-        mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
-        tma_load_3d(st, &tm_P, fb, j * kTile, m0, h, pol_p);
-        tma_load_3d(st + kBoxBytes, &tm_P, fb, j * kTile + kBoxCols, m0, h, pol_p);
+        if (j >= SV && !mbar_wait(&bar[kQbVEmpty0 + j % SV], ((j / SV) - 1) & 1, ctx, 1)) break;
+        {
+          uint64_t* fb = &bar[kQbVFull0 + j % SV];
+          uint8_t* dst = smem + Cfg::kOffV + (j % SV) * Cfg::kMD;
+          mbar_arrive_expect_tx(fb, Cfg::kMD);
 #pragma unroll
-        for (int b = 0; b < D / kBoxCols; ++b) {
-          tma_load_3d(st + Cfg::kPT + b * kBoxBytes, &tm_V, fb, b * kBoxCols, j * kTile, h, pol_kv);
-          tma_load_3d(st + Cfg::kPT + Cfg::kMD + b * kBoxBytes, &tm_K, fb, b * kBoxCols, j * kTile, h,
-                      pol_kv);
+          for (int b = 0; b < D / kBoxCols; ++b)
+            tma_load_3d(dst + b * kBoxBytes, &tm_V, fb, b * kBoxCols, j * kTile, h, pol_kv);
+          ++nV;
         }
-        ++issued;
+        if (j >= SP && !mbar_wait(&bar[kQbPEmpty0 + j % SP], ((j / SP) - 1) & 1, ctx, 2)) break;
+        {
+          uint64_t* fb = &bar[kQbPFull0 + j % SP];
+          uint8_t* dst = smem + Cfg::kOffP + (j % SP) * Cfg::kPT;
+          mbar_arrive_expect_tx(fb, Cfg::kPT);
+          tma_load_3d(dst, &tm_P, fb, j * kTile, m0, h, pol_p);
+          tma_load_3d(dst + kBoxBytes, &tm_P, fb, j * kTile + kBoxCols, m0, h, pol_p);
+          ++nP;
+        }
+        if (j >= SK && !mbar_wait(&bar[kQbKEmpty0 + j % SK], ((j / SK) - 1) & 1, ctx, 3)) break;
+        {
+          uint64_t* fb = &bar[kQbKFull0 + j % SK];
+          uint8_t* dst = smem + Cfg::kOffK + (j % SK) * Cfg::kMD;
+          mbar_arrive_expect_tx(fb, Cfg::kMD);
+#pragma unroll
+          for (int b = 0; b < D / kBoxCols; ++b)
+            tma_load_3d(dst + b * kBoxBytes, &tm_K, fb, b * kBoxCols, j * kTile, h, pol_kv);
+          ++nK;
+        }
       }
       if (*abort_flag) {
+        // let every copy still in flight land before the CTA exits
         mbar_wait_drain(&bar[kQbDO], 0, timeout_ns);
-        for (int j = (issued > S ? issued - S : 0); j < issued; ++j)
-          mbar_wait_drain(&bar[kQbFull0 + j % S], (j / S) & 1, timeout_ns);
+        for (int j = (nV > SV ? nV - SV : 0); j < nV; ++j)
+          mbar_wait_drain(&bar[kQbVFull0 + j % SV], (j / SV) & 1, timeout_ns);
+        for (int j = (nP > SP ? nP - SP : 0); j < nP; ++j)
+          mbar_wait_drain(&bar[kQbPFull0 + j % SP], (j / SP) & 1, timeout_ns);
+        for (int j = (nK > SK ? nK - SK : 0); j < nK; ++j)
+          mbar_wait_drain(&bar[kQbKFull0 + j % SK], (j / SK) & 1, timeout_ns);
       }
     }
-  } else if (warp == 1) {
-    // ---- MMA issuer. Order: dP_0 B_0 dP_1 | A_0 B_1 dP_2 | A_1 B_2 dP_3 | ...
+  } else if (warp == 1 || warp == Cfg::kAbWarp) {
+    // ---- Two MMA issuers. The tensor pipe accepts only about one
+    // instruction ahead of the one executing, so a single issuing thread
+    // leaves it idle at every wait; with two, one keeps it fed while the
+    // other waits. Warp 1: dP_j = dO_i V_j^T into X_(j%2). Warp kAbWarp:
+    // B_j += P_ij K_j, then A_j += E_ij K_j (E from TMEM).
     if (lane == 0) {
       constexpr bool kB = Elem<T>::kBF16;
       // dP = dO_i V_j^T: A = dO_i (K-major over d), B = V_j (K-major over d)
@@ -275,61 +321,62 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       // A += E K_j, B += P K_j: K = keys, N = d; B operand K_j [key][d] is MN-major
       constexpr uint32_t id_AB = make_idesc_f16<kB>(kTile, D, false, true);
       const uint32_t sdO = smem_u32(smem + Cfg::kOffdO);
-      auto stage_addr = [&](int j) {
-        return smem_u32(smem + Cfg::kOffStage + (j % S) * Cfg::kStageBytes);
-      };
-      auto issue_dP = [&](int j) -> bool {
-        if (!mbar_wait(&bar[kQbFull0 + j % S], (j / S) & 1, ctx, 10)) return false;
-        if (j >= 2 && !mbar_wait(&bar[kQbXFree0 + (j & 1)], ((j >> 1) - 1) & 1, ctx, 11)) return false;
-        tc_fence_after();
-        const uint32_t sV = stage_addr(j) + Cfg::kPT;
-        const uint32_t tX = tmem + Cfg::kColX + 128 * (j & 1);
+      const uint32_t sV0 = smem_u32(smem + Cfg::kOffV);
+      const uint32_t sK0 = smem_u32(smem + Cfg::kOffK);
+      const uint32_t sP0 = smem_u32(smem + Cfg::kOffP);
+      bool ok = true;
+      if (warp == 1) {
+        ok = mbar_wait(&bar[kQbDO], 0, ctx, 13);
+        for (int j = 0; j < nt && ok; ++j) {
+          if (!mbar_wait(&bar[kQbVFull0 + j % SV], (j / SV) & 1, ctx, 10)) { ok = false; break; }
+          if (j >= 2 && !mbar_wait(&bar[kQbXFree0 + (j & 1)], ((j >> 1) - 1) & 1, ctx, 11)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sV = sV0 + (j % SV) * Cfg::kMD;
+          const uint32_t tX = tmem + Cfg::kColX + 128 * (j & 1);
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k >> 2) * kBoxBytes + (k & 3) * 32;
-          umma_f16_ss(tX, make_sw128_desc(sdO + off, 16, 1024), make_sw128_desc(sV + off, 16, 1024), id_dP,
-                      k > 0 ? 1u : 0u);
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t off = (k >> 2) * kBoxBytes + (k & 3) * 32;
+            umma_f16_ss(tX, make_sw128_desc(sdO + off, 16, 1024), make_sw128_desc(sV + off, 16, 1024), id_dP,
+                        k > 0 ? 1u : 0u);
+          }
+          umma_commit(&bar[kQbXFull0 + (j & 1)]);
+          umma_commit(&bar[kQbVEmpty0 + j % SV]);  // V_j consumed
         }
-        umma_commit(&bar[kQbXFull0 + (j & 1)]);
-        return true;
-      };
-      auto issue_B = [&](int j) {
-        const uint32_t sP = stage_addr(j);
-        const uint32_t sK = sP + Cfg::kPT + Cfg::kMD;
-#pragma unroll
-        for (int k = 0; k < kTile / 16; ++k) {
-          umma_f16_ss(tmem + Cfg::kColB, make_sw128_desc(sP + (k >> 2) * kBoxBytes + (k & 3) * 32, 16, 1024),
-                      make_sw128_desc(sK + k * 2048, kBoxBytes, 1024), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+        if (!ok) {
+          umma_commit(&bar[kQbDrain]);
+          mbar_wait_drain(&bar[kQbDrain], 0, timeout_ns);
         }
-      };
-      auto issue_A = [&](int j) -> bool {
-        if (!mbar_wait(&bar[kQbEFull0 + (j & 1)], (j >> 1) & 1, ctx, 12)) return false;
-        tc_fence_after();
-        const uint32_t sK = stage_addr(j) + Cfg::kPT + Cfg::kMD;
-        const uint32_t tE = tmem + Cfg::kColX + 128 * (j & 1);
-#pragma unroll
-        for (int k = 0; k < kTile / 16; ++k) {
-          // E for keys 16k..16k+15 sits in key half (k >> 2): 8 columns per step
-          umma_f16_ts(tmem + Cfg::kColA, tE + (k >> 2) * 64 + (k & 3) * 8,
-                      make_sw128_desc(sK + k * 2048, kBoxBytes, 1024), id_AB, (j > 0 || k > 0) ? 1u : 0u);
-        }
-        umma_commit(&bar[kQbEmpty0 + j % S]);  // stage j: V (dP_j), P and K (B_j, A_j) consumed
-        umma_commit(&bar[kQbXFree0 + (j & 1)]);
-        return true;
-      };
-      bool ok = mbar_wait(&bar[kQbDO], 0, ctx, 13) && issue_dP(0);
-      if (ok) issue_B(0);
-      if (ok && nt > 1) ok = issue_dP(1);
-      for (int j = 0; j < nt && ok; ++j) {
-        if (!issue_A(j)) { ok = false; break; }
-        if (j + 1 < nt) issue_B(j + 1);
-        if (j + 2 < nt && !issue_dP(j + 2)) { ok = false; break; }
-      }
-      if (ok) {
-        umma_commit(&bar[kQbAB]);
       } else {
-        umma_commit(&bar[kQbDrain]);
-        mbar_wait_drain(&bar[kQbDrain], 0, timeout_ns);
+        for (int j = 0; j < nt && ok; ++j) {
+          if (!mbar_wait(&bar[kQbPFull0 + j % SP], (j / SP) & 1, ctx, 14)) { ok = false; break; }
+          if (!mbar_wait(&bar[kQbKFull0 + j % SK], (j / SK) & 1, ctx, 15)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sP = sP0 + (j % SP) * Cfg::kPT;
+          const uint32_t sK = sK0 + (j % SK) * Cfg::kMD;
+#pragma unroll
+          for (int k = 0; k < kTile / 16; ++k) {
+            umma_f16_ss(tmem + Cfg::kColB, make_sw128_desc(sP + (k >> 2) * kBoxBytes + (k & 3) * 32, 16, 1024),
+                        make_sw128_desc(sK + k * 2048, kBoxBytes, 1024), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&bar[kQbPEmpty0 + j % SP]);  // the tensor core's read of P_ij
+          if (!mbar_wait(&bar[kQbEFull0 + (j & 1)], (j >> 1) & 1, ctx, 12)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t tE = tmem + Cfg::kColX + 128 * (j & 1);
+#pragma unroll
+          for (int k = 0; k < kTile / 16; ++k) {
+            // E for keys 16k..16k+15 sits in key half (k >> 2): 8 columns per step
+            umma_f16_ts(tmem + Cfg::kColA, tE + (k >> 2) * 64 + (k & 3) * 8,
+                        make_sw128_desc(sK + k * 2048, kBoxBytes, 1024), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&bar[kQbKEmpty0 + j % SK]);  // K_j consumed (B_j and A_j)
+          umma_commit(&bar[kQbXFree0 + (j & 1)]);
+        }
+        if (ok) {
+          umma_commit(&bar[kQbAB]);
+        } else {
+          umma_commit(&bar[kQbDrain2]);
+          mbar_wait_drain(&bar[kQbDrain2], 0, timeout_ns);
+        }
       }
     }
   } else {
@@ -365,16 +412,16 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
     };
     bool ok = true;
     for (int j = 0; j < nt && ok; ++j) {
-      const int s = j % S;
+      const int s = j % SP;
       const int b = j & 1;
       if (!mbar_wait(&bar[kQbXFull0 + b], (j >> 1) & 1, ctx, 20)) { ok = false; break; }
-      if (!mbar_wait(&bar[kQbFull0 + s], (j / S) & 1, ctx, 21)) { ok = false; break; }
+      if (!mbar_wait(&bar[kQbPFull0 + s], (j / SP) & 1, ctx, 21)) { ok = false; break; }
       __syncwarp();
       tc_fence_after();
       uint32_t dpa[32], dpb[32];
       tmem_load_32(lane_base + Cfg::kColX + 128 * b + 64 * c, dpa);
       tmem_load_32(lane_base + Cfg::kColX + 128 * b + 64 * c + 32, dpb);
-      const uint8_t* pbox = smem + Cfg::kOffStage + s * Cfg::kStageBytes + c * kBoxBytes;
+      const uint8_t* pbox = smem + Cfg::kOffP + s * Cfg::kPT + c * kBoxBytes;
       uint4 pv[8];
 #pragma unroll
       for (int x = 0; x < 8; ++x) pv[x] = *reinterpret_cast<const uint4*>(pbox + sw128_offset(rsw, x));
@@ -416,7 +463,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&bar[kQbEFull0 + b]);
-        mbar_arrive(&bar[kQbEmpty0 + s]);
+        mbar_arrive(&bar[kQbPEmpty0 + s]);
       }
     }
     // dQ = A - (D - c) B, and D
@@ -446,6 +493,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) publish_failure(*abort_flag, status);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
@@ -548,7 +596,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  WaitCtx ctx{abort_flag, status, timeout_ns};
+  WaitCtx ctx{abort_flag, timeout_ns};
 
   if (warp == 0) {
     // ---- TMA producer: V_j once, then the P stream (2 stages).
@@ -640,7 +688,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         } else {
           if (*abort_flag) break;
           if (global_timer_ns() - t_last > timeout_ns) {
-            record_failure(ctx, kStatusWaitTimeout, 31);
+            note_failure(ctx, 31);
             failed = true;
           }
         }
@@ -785,6 +833,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) publish_failure(*abort_flag, status);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);

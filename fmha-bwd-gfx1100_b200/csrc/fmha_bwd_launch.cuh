@@ -88,14 +88,15 @@ inline EncodeTiledFn encode_fn() {
 }
 
 // 3-D map over a [heads][rows][cols] row-major 16-bit tensor, box of
-// 64 columns x 128 rows x 1 head, 128-byte swizzle, zero fill out of bounds.
+// 64 columns x `box_rows` rows x 1 head, 128-byte swizzle, zero fill out of
+// bounds.
 inline bool encode_map(CUtensorMap* map, bool bf16, const void* base, uint64_t cols,
-                       uint64_t rows, uint64_t heads) {
+                       uint64_t rows, uint64_t heads, uint32_t box_rows = kTile) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[3] = {cols, rows, heads};
   const cuuint64_t strides[2] = {cols * 2, rows * cols * 2};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kBoxCols), static_cast<cuuint32_t>(kTile), 1};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kBoxCols), box_rows, 1};
   const cuuint32_t elem[3] = {1, 1, 1};
   CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
                   const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -160,22 +161,29 @@ void set_kernel_attrs() {
                        DkvCfg<128>::kSmemBytes);
 }
 
+// The status slot of `device`, allocated on first use (caller holds
+// ws_mutex). Returns false (error recorded) if the allocation fails.
+inline bool ensure_status_slot(int device, DeviceWorkspace& w) {
+  if (!w.host_status) {
+    if (cudaHostAlloc(&w.host_status, sizeof(KernelStatus),
+                      cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess ||
+        cudaHostGetDevicePointer(&w.host_status_dev, w.host_status, 0) != cudaSuccess) {
+      set_error(kErrOutOfMemory, "host status slot allocation failed");
+      return false;
+    }
+    memset(w.host_status, 0, sizeof(KernelStatus));
+    cudaDeviceGetAttribute(&w.sm_count, cudaDevAttrMultiProcessorCount, device);
+  }
+  return true;
+}
+
 // Returns the workspace of the current device with at least the requested
 // capacity, or nullptr (error already recorded).
 template <typename T>
 DeviceWorkspace* get_workspace(int device, size_t dsum_floats) {
   std::lock_guard<std::mutex> g(ws_mutex());
   DeviceWorkspace& w = ws_map()[device];
-  if (!w.host_status) {
-    if (cudaHostAlloc(&w.host_status, sizeof(KernelStatus),
-                      cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess ||
-        cudaHostGetDevicePointer(&w.host_status_dev, w.host_status, 0) != cudaSuccess) {
-      set_error(kErrOutOfMemory, "host status slot allocation failed");
-      return nullptr;
-    }
-    memset(w.host_status, 0, sizeof(KernelStatus));
-    cudaDeviceGetAttribute(&w.sm_count, cudaDevAttrMultiProcessorCount, device);
-  }
+  if (!ensure_status_slot(device, w)) return nullptr;
   if (!w.attrs_set) {
     set_kernel_attrs<T>();
     w.attrs_set = true;
@@ -228,6 +236,71 @@ inline int check_args(const void* dQ, const void* dK, const void* dV, const void
   return kOk;
 }
 
+// Encodes the tensor maps and enqueues the two kernels on `stream`, with D
+// at `dsum` and the wait status at `st`. Arguments are already checked.
+// Optional timing events: [0] before the dQ kernel, [1] between the two
+// kernels, [2] and [3] after the dK/dV kernel.
+template <typename T>
+int enqueue_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const T* P,
+                     const T* dO, int M, int N, int D, int H, float* dsum, KernelStatus* st,
+                     cudaStream_t stream, cudaEvent_t const* events) {
+  constexpr bool kBF16 = Elem<T>::kBF16;
+  CUtensorMap mQ, mK, mV, mdO, mP;
+  if (!encode_fn()) return set_error(kErrNoDriver, "cuTensorMapEncodeTiled is unavailable");
+  if (!encode_map(&mQ, kBF16, Q, D, M, H) || !encode_map(&mK, kBF16, K, D, N, H) ||
+      !encode_map(&mV, kBF16, V, D, N, H) ||
+      !encode_map(&mdO, kBF16, dO, D, M, H) || !encode_map(&mP, kBF16, P, N, M, H))
+    return set_error(kErrInvalidArgument, "tensor map encoding failed (M=%d N=%d K_dim=%d heads=%d)",
+                     M, N, D, H);
+  const uint64_t tmo = effective_timeout_ns();
+  auto mark = [&](int k) {
+    if (events && events[k]) cudaEventRecord(events[k], stream);
+  };
+  const int mt = (M + kTile - 1) / kTile;
+  const dim3 grid_rows(mt, H);
+  const dim3 grid_cols((N + kTile - 1) / kTile, H);
+  mark(0);
+  if (D == 128) {
+    dq_kernel<T, 128><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
+        mP, mV, mK, mdO, dQ, dsum, M, N, st, tmo);
+    mark(1);
+    dkv_kernel<T, 128><<<grid_cols, DkvCfg<128>::kThreads, DkvCfg<128>::kSmemBytes, stream>>>(
+        mQ, mV, mdO, mP, dsum, dK, dV, M, N, st, tmo);
+  } else {
+    dq_kernel<T, 64><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
+        mP, mV, mK, mdO, dQ, dsum, M, N, st, tmo);
+    mark(1);
+    dkv_kernel<T, 64><<<grid_cols, DkvCfg<64>::kThreads, DkvCfg<64>::kSmemBytes, stream>>>(
+        mQ, mV, mdO, mP, dsum, dK, dV, M, N, st, tmo);
+  }
+  mark(2);
+  mark(3);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(kErrLaunch, "launch failed: %s", cudaGetErrorString(e));
+  return kOk;
+}
+
+// Self-test of the bounded-wait machinery: one warp waits on an mbarrier that
+// nothing ever arrives on. The wait gives up after `timeout_ns`, records
+// (kStatusWaitTimeout, kSelfTestSite) in the status slot and the kernel
+// returns normally.
+constexpr int kSelfTestSite = 99;
+__global__ void wait_selftest_kernel(KernelStatus* status, uint64_t timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    WaitCtx ctx{reinterpret_cast<volatile int*>(&abort_flag), timeout_ns};
+    mbar_wait(&bar, 0, ctx, kSelfTestSite);
+    publish_failure(abort_flag, status);
+  }
+}
+
 // Launches the two kernels on `stream`. When `sync` is set, waits for the
 // stream and reports in-kernel wait timeouts as kErrDeviceTimeout.
 template <typename T>
@@ -251,43 +324,11 @@ int run_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const 
   DeviceWorkspace* w = get_workspace<T>(device, rows);
   if (!w) return kErrOutOfMemory;
 
-  constexpr bool kBF16 = Elem<T>::kBF16;
-  CUtensorMap mQ, mK, mV, mdO, mP;
-  if (!encode_fn()) return set_error(kErrNoDriver, "cuTensorMapEncodeTiled is unavailable");
-  if (!encode_map(&mQ, kBF16, Q, D, M, H) || !encode_map(&mK, kBF16, K, D, N, H) ||
-      !encode_map(&mV, kBF16, V, D, N, H) || !encode_map(&mdO, kBF16, dO, D, M, H) ||
-      !encode_map(&mP, kBF16, P, N, M, H))
-    return set_error(kErrInvalidArgument, "tensor map encoding failed (M=%d N=%d K_dim=%d heads=%d)",
-                     M, N, D, H);
-
   if (sync) memset(w->host_status, 0, sizeof(KernelStatus));
-  const uint64_t tmo = effective_timeout_ns();
-  // Optional timing events at the kernel boundaries: [0] before dq_kernel,
-  // [1] between the two kernels, [2] and [3] after dkv_kernel.
-  auto mark = [&](int k) {
-    if (events && events[k]) cudaEventRecord(events[k], stream);
-  };
-  const dim3 grid_rows((M + kTile - 1) / kTile, H);
-  const dim3 grid_cols((N + kTile - 1) / kTile, H);
-  KernelStatus* st = w->host_status_dev;
-  mark(0);
-  if (D == 128) {
-    dq_kernel<T, 128><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
-        mP, mV, mK, mdO, dQ, w->dsum, M, N, st, tmo);
-    mark(1);
-    dkv_kernel<T, 128><<<grid_cols, DkvCfg<128>::kThreads, DkvCfg<128>::kSmemBytes, stream>>>(
-        mQ, mV, mdO, mP, w->dsum, dK, dV, M, N, st, tmo);
-  } else {
-    dq_kernel<T, 64><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
-        mP, mV, mK, mdO, dQ, w->dsum, M, N, st, tmo);
-    mark(1);
-    dkv_kernel<T, 64><<<grid_cols, DkvCfg<64>::kThreads, DkvCfg<64>::kSmemBytes, stream>>>(
-        mQ, mV, mdO, mP, w->dsum, dK, dV, M, N, st, tmo);
-  }
-  mark(2);
-  mark(3);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_error(kErrLaunch, "launch failed: %s", cudaGetErrorString(e));
+  rc = enqueue_backward<T>(dQ, dK, dV, Q, K, V, P, dO, M, N, D, H, w->dsum, w->host_status_dev,
+                           stream, events);
+  if (rc != kOk) return rc;
+  cudaError_t e = cudaSuccess;
   if (sync) {
     e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess) return set_error(kErrLaunch, "kernel failed: %s", cudaGetErrorString(e));

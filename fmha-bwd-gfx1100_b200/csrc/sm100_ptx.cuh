@@ -74,6 +74,20 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_test, with cluster-scope acquire: for barriers that the other CTA
+// of a pair arrives on (remote arrivals, TMA completions, MMA commits).
+__device__ __forceinline__ bool mbar_test_cl(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Non-blocking probe of a phase (never suspends the thread).
 __device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -87,33 +101,41 @@ __device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Shared per-CTA abort flag lives in shared memory; once any role gives up,
-// the others stop waiting too.
+// Per-CTA abort flag in shared memory: 0 while every wait succeeds, else
+// 1 + the site id of the first wait that gave up. Once it is set the other
+// roles of the CTA stop waiting too. Waits only touch this flag; the global
+// status record is written once, at the end of the kernel, by
+// publish_failure (keeping fences and global stores out of the loops that
+// issue tensor-core work, where even an untaken path with them slows the
+// issue of tcgen05.mma).
 struct WaitCtx {
   volatile int* abort_flag;  // shared memory
-  KernelStatus* status;      // global memory
   uint64_t timeout_ns;
 };
 
-// `status` points at pinned, device-mapped host memory, so the host reads it
-// after the stream finishes without a copy. Concurrent writers may
-// interleave; any one failure record is enough.
-__device__ __noinline__ void record_failure(const WaitCtx& ctx, int code,
-                                            int where) {
-  *ctx.abort_flag = 1;
-  volatile KernelStatus* st = ctx.status;
+__device__ __forceinline__ void note_failure(const WaitCtx& ctx, int where) {
+  if (*ctx.abort_flag == 0) *ctx.abort_flag = 1 + where;
+}
+
+// Called by one thread per CTA after all roles have finished. `status`
+// points at pinned, device-mapped host memory (or a device array), read by
+// the host after the stream finishes; the first failing CTA's record wins
+// (concurrent writers may interleave; any one record is enough).
+__device__ __noinline__ void publish_failure(int abort_value, KernelStatus* status) {
+  if (abort_value == 0) return;
+  volatile KernelStatus* st = status;
   if (st->code == 0) {
-    st->where = where;
+    st->where = abort_value - 1;
     st->block =
         static_cast<int>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
     __threadfence_system();
-    st->code = code;
+    st->code = kStatusWaitTimeout;
   }
 }
 
-// Bounded wait for the phase with the given parity. Returns false (and
-// records why) if the phase does not complete within ctx.timeout_ns or if
-// another role of this CTA has already aborted.
+// Bounded wait for the phase with the given parity. Returns false (and notes
+// the site) if the phase does not complete within ctx.timeout_ns, or at once
+// if another role of this CTA has already given up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           const WaitCtx& ctx, int where) {
   if (mbar_test(bar, parity)) return true;
@@ -122,14 +144,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     if (mbar_test(bar, parity)) return true;
     if ((it & 63u) == 63u) {
       if (*ctx.abort_flag) return false;
-      if (global_timer_ns() - t0 > ctx.timeout_ns) {
-        record_failure(ctx, kStatusWaitTimeout, where);
+      if (global_timer_ns() - t0 > ctx.timeout_ns || it > (1u << 30)) {
+        note_failure(ctx, where);
         return false;
       }
     }
-    if (it > (1u << 30)) {  // iteration cap, independent of the timer
-      record_failure(ctx, kStatusWaitTimeout, where);
-      return false;
+  }
+}
+
+// mbar_wait with cluster-scope acquire (see mbar_test_cl).
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity,
+                                             const WaitCtx& ctx, int where) {
+  if (mbar_test_cl(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_test_cl(bar, parity)) return true;
+    if ((it & 63u) == 63u) {
+      if (*ctx.abort_flag) return false;
+      if (global_timer_ns() - t0 > ctx.timeout_ns || it > (1u << 30)) {
+        note_failure(ctx, where);
+        return false;
+      }
     }
   }
 }
@@ -296,6 +331,101 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem,
 // Named barrier over `count` threads (id 1..15; id 0 is __syncthreads).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// --------------------------------------------- CTA pairs (2-SM tcgen05 MMA)
+// A cluster of two CTAs on two SMs runs one M = 256 MMA: each CTA holds its
+// 128 rows of A (and of the accumulator, in its own TMEM) and half of the N
+// rows of B, at the same shared-memory / TMEM offsets; CTA rank 0 (the
+// leader) issues the MMAs. Every tcgen05 instruction of such a kernel uses
+// .cta_group::2.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the variable at shared::cta address `addr` in
+// CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// All threads of both CTAs (release/acquire at cluster scope). The
+// non-.aligned forms: threads of a warp may arrive at different times.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\t"
+               "barrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (may be in the
+// other CTA of the pair).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+// TMA load into this CTA's shared memory whose completion (transaction
+// bytes) is reported on an mbarrier of either CTA of the pair, given by its
+// shared::cluster address. No multicast.
+__device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const void* tmap,
+                                                 uint32_t bar_cluster_addr, int x, int y, int z,
+                                                 uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster_addr), "r"(x), "r"(y), "r"(z),
+      "l"(cache_hint)
+      : "memory");
+}
+
+// One warp of EACH CTA of the pair (same warp index) executes these.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile(
+      "tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+          smem_u32(smem_result)),
+      "r"(ncols)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" :: : "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// Pair MMA, A and B from shared memory (issued by the leader only).
+__device__ __forceinline__ void umma2_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Pair MMA, A from TMEM (each CTA's own 128 rows), B from shared memory.
+__device__ __forceinline__ void umma2_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the mbarrier at `cluster_addr` (either CTA of the pair) when
+// every pair MMA issued so far by this thread has completed.
+__device__ __forceinline__ void umma2_commit(uint32_t cluster_addr) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          cluster_addr)
+      : "memory");
 }
 
 // ------------------------------------------------------- UMMA descriptors

@@ -144,6 +144,13 @@ const char* fmha_bwd_last_error_message(void);
  * FMHA_BWD_ERR_DEVICE_TIMEOUT. Call after synchronising the stream. */
 int fmha_bwd_poll_device_status(void);
 
+/* No counterpart in the reference. Self-test of the bounded in-kernel waits:
+ * launches one warp that waits on a barrier nothing arrives on, with a limit
+ * of `timeout_ms` (1..10000). Returns FMHA_BWD_OK if the wait gave up, the
+ * timeout was recorded in the status slot and the kernel exited normally (the
+ * context stays usable); otherwise an error code. Synchronises the device. */
+int fmha_bwd_selftest_wait_timeout(int timeout_ms);
+
 /* Upper bound, in milliseconds, on any single in-kernel wait (default 4000,
  * or FMHA_BWD_WAIT_TIMEOUT_MS). A wait that runs out sets the device status
  * word and the kernel drains and exits instead of hanging. 0 restores the

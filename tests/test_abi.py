@@ -121,3 +121,14 @@ def test_python_mirror_fails_loudly_without_cuda_tensors():
         F.fmha_bwd(x, x, x, torch.zeros(1, 128, 128, dtype=torch.bfloat16), x)
     with pytest.raises(TypeError):
         F.library_path(torch.float32)
+
+
+@pytest.mark.parametrize("kind", ["bf16", "fp16"])
+def test_selftest_rejects_bad_timeout_without_gpu(kind):
+    _ensure_built()
+    lib = ctypes.CDLL(LIBS[kind])
+    f = lib.fmha_bwd_selftest_wait_timeout
+    f.argtypes = [ctypes.c_int]
+    f.restype = ctypes.c_int
+    assert f(0) == 1
+    assert f(20000) == 1

@@ -203,3 +203,25 @@ def test_bad_device_pointer_layout_rejected(F):
     with pytest.raises(F.FmhaBwdError) as e:
         F.fmha_bwd(odd, Kk, Kk, Pk, x)
     assert e.value.code == 2
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_bounded_wait_gives_up_and_context_survives(F, oracle_built, dtype):
+    """A kernel waiting on a barrier nothing arrives on gives up after 50 ms,
+    records the timeout in the status slot and exits; the same context then
+    runs a real backward that matches the oracle."""
+    import ctypes
+
+    lib = F.load_library(dtype)
+    lib.fmha_bwd_selftest_wait_timeout.argtypes = [ctypes.c_int]
+    lib.fmha_bwd_selftest_wait_timeout.restype = ctypes.c_int
+    assert lib.fmha_bwd_selftest_wait_timeout(50) == 0, lib.fmha_bwd_last_error_message()
+    assert lib.fmha_bwd_poll_device_status() == 0  # the self-test cleared its record
+    O = oracle_built
+    name = "bf16" if dtype == torch.bfloat16 else "fp16"
+    Qb, Kb, Vb, Pb, dOb = O.make_inputs(256, 128, 64, 2, name, seed=31)
+    ins = [_to_dev(x, dtype) for x in (Qb, Kb, Vb, Pb, dOb)]
+    dQ, dK, dV = F.fmha_bwd(*ins)
+    ref = O.oracle_bwd(Qb, Kb, Vb, Pb, dOb, name)
+    for nm, got, r in zip(("dQ", "dK", "dV"), (dQ, dK, dV), ref[:3]):
+        _assert_ok(O, nm, _f32(got), r, name)
