@@ -502,12 +502,13 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 
 // =============================================================== dkv_kernel
 // Shared memory (D = 128): V_j 32 KB, P_ij x2 64 KB, dS 32 KB, dO_i x2 64 KB,
-// Q_i 32 KB = 224 KB. TMEM: dP [0,128) (lane = query row, column = key),
-// dV [128,128+D) and dK [128+D,128+2D) (lane = key row, column = d).
+// Q_i 32 KB = 224 KB. TMEM: two dP buffers [0,256) (lane = query row, column
+// = key), dV [256,256+D) and dK [256+D,256+2D) (lane = key row, column = d).
 //
-// Warp roles (12 warps): 0 TMA for V_j and the P stream; 1 MMA issuer (and
-// TMEM owner); 2 TMA for dO_i and Q_i; 3 idle; 4-11 dS warps (TMEM lane
-// quarter = warp % 4, key half = (warp - 4) / 4), which also write dK_j, dV_j.
+// Warp roles (12 warps): 0 TMA for V_j and the P stream; 1 MMA issuer for
+// dP (and TMEM owner); 2 TMA for dO_i and Q_i; 3 MMA issuer for dV and dK;
+// 4-11 dS warps (TMEM lane quarter = warp % 4, key half = (warp - 4) / 4),
+// which also write dK_j, dV_j.
 template <int D>
 struct DkvCfg {
   static constexpr int kMD = (D / kBoxCols) * kBoxBytes;
@@ -523,10 +524,10 @@ struct DkvCfg {
   static constexpr int kDSWarps = 8;
   static constexpr int kFirstDSWarp = 4;
   static constexpr int kThreads = 32 * (kFirstDSWarp + kDSWarps);
-  static constexpr uint32_t kTmemCols = D == 128 ? 512 : 256;
-  static constexpr uint32_t kColdP = 0;
-  static constexpr uint32_t kColdV = 128;
-  static constexpr uint32_t kColdK = 128 + D;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kColdP = 0;  // + 128 * buffer (two dP buffers)
+  static constexpr uint32_t kColdV = 256;
+  static constexpr uint32_t kColdK = 256 + D;
   static_assert(kColdK + D <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -539,13 +540,14 @@ enum DkvBar : int {
   kKbDOEmpty0 = 7,
   kKbQFull = 9,
   kKbQEmpty = 10,
-  kKbDPFull = 11,
-  kKbDPEmpty = 12,
-  kKbDSFull = 13,
-  kKbDSEmpty = 14,
-  kKbAcc = 15,
-  kKbDrain = 16,
-  kNumDkvBars = 17,
+  kKbDPFull0 = 11,   // + dP buffer (2)
+  kKbDPEmpty0 = 13,  // + dP buffer
+  kKbDSFull = 15,
+  kKbDSEmpty = 16,
+  kKbAcc = 17,
+  kKbDrain = 18,
+  kKbDrain2 = 19,
+  kNumDkvBars = 20,
 };
 
 template <typename T, int D>
@@ -575,16 +577,19 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       mbar_init(&bar[kKbPFull0 + s], 1);
       mbar_init(&bar[kKbPEmpty0 + s], 1 + kEpi);
       mbar_init(&bar[kKbDOFull0 + s], 1);
-      mbar_init(&bar[kKbDOEmpty0 + s], 1);
+      mbar_init(&bar[kKbDOEmpty0 + s], 2);  // read by dP_i and dV_i (two issuers)
     }
     mbar_init(&bar[kKbQFull], 1);
     mbar_init(&bar[kKbQEmpty], 1);
-    mbar_init(&bar[kKbDPFull], 1);
-    mbar_init(&bar[kKbDPEmpty], kEpi);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar[kKbDPFull0 + b], 1);
+      mbar_init(&bar[kKbDPEmpty0 + b], kEpi);
+    }
     mbar_init(&bar[kKbDSFull], kEpi);
     mbar_init(&bar[kKbDSEmpty], 1);
     mbar_init(&bar[kKbAcc], 1);
     mbar_init(&bar[kKbDrain], 1);
+    mbar_init(&bar[kKbDrain2], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -699,9 +704,11 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         if (next_q > 0) mbar_wait_drain(&bar[kKbQFull], (next_q - 1) & 1, timeout_ns);
       }
     }
-  } else if (warp == 1) {
-    // ---- MMA issuer. Order: dP_0 dV_0 | dP_1 dV_1 dK_0 | dP_2 dV_2 dK_1 | ...
-    // so the dS epilogue of tile i overlaps dK_{i-1}, dP_{i+1} and dV_{i+1}.
+  } else if (warp == 1 || warp == 3) {
+    // ---- Two MMA issuers (one keeps the tensor pipe fed while the other
+    // waits). Warp 1: dP_i = dO_i V_j^T. Warp 3: dV_j += P_ij^T dO_i and
+    // dK_j += dS_ij^T Q_i in the order dV_0 dV_1 dK_0 dV_2 dK_1 ..., so the
+    // dS epilogue of tile i overlaps dV_{i+1}.
     if (lane == 0) {
       constexpr bool kB = Elem<T>::kBF16;
       constexpr uint32_t id_dP = make_idesc_f16<kB>(kTile, kTile, false, false);
@@ -709,57 +716,73 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       const uint32_t sV = smem_u32(smem + Cfg::kOffV);
       const uint32_t sS = smem_u32(smem + Cfg::kOffS);
       const uint32_t sQ = smem_u32(smem + Cfg::kOffQ);
-      auto issue_dP_dV = [&](int i) -> bool {
-        const int s = i & 1;
-        const uint32_t sdO = smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD);
-        const uint32_t sP = smem_u32(smem + Cfg::kOffP + s * Cfg::kPT);
-        // dP = dO_i V_j^T : A = dO_i (K-major over d), B = V_j (K-major over d).
-        if (!mbar_wait(&bar[kKbDOFull0 + s], (i >> 1) & 1, ctx, 40)) return false;
-        if (i > 0) {
-          if (!mbar_wait(&bar[kKbDPEmpty], (i - 1) & 1, ctx, 41)) return false;
+      bool ok = true;
+      if (warp == 1) {
+        ok = mbar_wait(&bar[kKbV], 0, ctx, 45);
+        for (int i = 0; i < mt && ok; ++i) {
+          const int s = i & 1;
+          const uint32_t sdO = smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD);
+          // dP = dO_i V_j^T : A = dO_i (K-major over d), B = V_j (K-major over d).
+          if (!mbar_wait(&bar[kKbDOFull0 + s], (i >> 1) & 1, ctx, 40)) { ok = false; break; }
+          // dP buffer b = i % 2 is free once the dS warps have read dP_{i-2}
+          if (i >= 2 && !mbar_wait(&bar[kKbDPEmpty0 + (i & 1)], ((i >> 1) - 1) & 1, ctx, 41)) { ok = false; break; }
           tc_fence_after();
-        }
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k >> 2) * kBoxBytes + (k & 3) * 32;
-          umma_f16_ss(tmem + Cfg::kColdP, make_sw128_desc(sdO + off, 16, 1024),
-                      make_sw128_desc(sV + off, 16, 1024), id_dP, k > 0 ? 1u : 0u);
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t off = (k >> 2) * kBoxBytes + (k & 3) * 32;
+            umma_f16_ss(tmem + Cfg::kColdP + 128 * (i & 1), make_sw128_desc(sdO + off, 16, 1024),
+                        make_sw128_desc(sV + off, 16, 1024), id_dP, k > 0 ? 1u : 0u);
+          }
+          umma_commit(&bar[kKbDPFull0 + (i & 1)]);
+          umma_commit(&bar[kKbDOEmpty0 + s]);
         }
-        umma_commit(&bar[kKbDPFull]);
-        // dV += P_ij^T dO_i : A = P^T (MN-major, M = key), B = dO_i (MN-major, N = d).
-        if (!mbar_wait(&bar[kKbPFull0 + s], (i >> 1) & 1, ctx, 42)) return false;
-#pragma unroll
-        for (int k = 0; k < kTile / 16; ++k) {
-          umma_f16_ss(tmem + Cfg::kColdV, make_sw128_desc(sP + k * 2048, kBoxBytes, 1024),
-                      make_sw128_desc(sdO + k * 2048, kBoxBytes, 1024), id_dVK, (i > 0 || k > 0) ? 1u : 0u);
+        if (!ok) {
+          umma_commit(&bar[kKbDrain]);
+          mbar_wait_drain(&bar[kKbDrain], 0, timeout_ns);
         }
-        umma_commit(&bar[kKbDOEmpty0 + s]);
-        umma_commit(&bar[kKbPEmpty0 + s]);
-        return true;
-      };
-      auto issue_dK = [&](int i) -> bool {
-        // dK += dS^T Q_i : A = dS^T (MN-major, M = key), B = Q_i (MN-major, N = d).
-        if (!mbar_wait(&bar[kKbQFull], i & 1, ctx, 43)) return false;
-        if (!mbar_wait(&bar[kKbDSFull], i & 1, ctx, 44)) return false;
-#pragma unroll
-        for (int k = 0; k < kTile / 16; ++k) {
-          umma_f16_ss(tmem + Cfg::kColdK, make_sw128_desc(sS + k * 2048, kBoxBytes, 1024),
-                      make_sw128_desc(sQ + k * 2048, kBoxBytes, 1024), id_dVK, (i > 0 || k > 0) ? 1u : 0u);
-        }
-        umma_commit(&bar[kKbQEmpty]);
-        umma_commit(&bar[kKbDSEmpty]);
-        return true;
-      };
-      bool ok = mbar_wait(&bar[kKbV], 0, ctx, 45) && issue_dP_dV(0);
-      for (int i = 0; i < mt && ok; ++i) {
-        if (i + 1 < mt && !issue_dP_dV(i + 1)) { ok = false; break; }
-        if (!issue_dK(i)) { ok = false; break; }
-      }
-      if (ok) {
-        umma_commit(&bar[kKbAcc]);
       } else {
-        umma_commit(&bar[kKbDrain]);
-        mbar_wait_drain(&bar[kKbDrain], 0, timeout_ns);
+        auto issue_dV = [&](int i) -> bool {
+          const int s = i & 1;
+          const uint32_t sdO = smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD);
+          const uint32_t sP = smem_u32(smem + Cfg::kOffP + s * Cfg::kPT);
+          // dV += P_ij^T dO_i : A = P^T (MN-major, M = key), B = dO_i (MN-major, N = d).
+          if (!mbar_wait(&bar[kKbPFull0 + s], (i >> 1) & 1, ctx, 42)) return false;
+          if (!mbar_wait(&bar[kKbDOFull0 + s], (i >> 1) & 1, ctx, 46)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < kTile / 16; ++k) {
+            umma_f16_ss(tmem + Cfg::kColdV, make_sw128_desc(sP + k * 2048, kBoxBytes, 1024),
+                        make_sw128_desc(sdO + k * 2048, kBoxBytes, 1024), id_dVK, (i > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&bar[kKbDOEmpty0 + s]);
+          umma_commit(&bar[kKbPEmpty0 + s]);
+          return true;
+        };
+        auto issue_dK = [&](int i) -> bool {
+          // dK += dS^T Q_i : A = dS^T (MN-major, M = key), B = Q_i (MN-major, N = d).
+          if (!mbar_wait(&bar[kKbQFull], i & 1, ctx, 43)) return false;
+          if (!mbar_wait(&bar[kKbDSFull], i & 1, ctx, 44)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < kTile / 16; ++k) {
+            umma_f16_ss(tmem + Cfg::kColdK, make_sw128_desc(sS + k * 2048, kBoxBytes, 1024),
+                        make_sw128_desc(sQ + k * 2048, kBoxBytes, 1024), id_dVK, (i > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&bar[kKbQEmpty]);
+          umma_commit(&bar[kKbDSEmpty]);
+          return true;
+        };
+        ok = issue_dV(0);
+        for (int i = 0; i < mt && ok; ++i) {
+          if (i + 1 < mt && !issue_dV(i + 1)) { ok = false; break; }
+          if (!issue_dK(i)) { ok = false; break; }
+        }
+        if (ok) {
+          umma_commit(&bar[kKbAcc]);
+        } else {
+          umma_commit(&bar[kKbDrain2]);
+          mbar_wait_drain(&bar[kKbDrain2], 0, timeout_ns);
+        }
       }
     }
   } else if (warp >= Cfg::kFirstDSWarp) {
@@ -774,19 +797,20 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       const int s = i & 1;
       const int m = i * kTile + r;
       const float Dm = (m < M) ? __ldg(Dsum + static_cast<int64_t>(h) * M + m) : 0.f;
-      if (!mbar_wait(&bar[kKbDPFull], i & 1, ctx, 50)) { ok = false; break; }
+      const int b = i & 1;
+      if (!mbar_wait(&bar[kKbDPFull0 + b], (i >> 1) & 1, ctx, 50)) { ok = false; break; }
       __syncwarp();
       tc_fence_after();
       // Both 32-column halves of this warp's dP segment are loaded before any
-      // other work, then the TMEM is released.
+      // other work, then the TMEM buffer is released.
       uint32_t dpa[32], dpb[32];
-      tmem_load_32(lane_base + Cfg::kColdP + c * 64, dpa);
-      tmem_load_32(lane_base + Cfg::kColdP + c * 64 + 32, dpb);
+      tmem_load_32(lane_base + Cfg::kColdP + 128 * b + c * 64, dpa);
+      tmem_load_32(lane_base + Cfg::kColdP + 128 * b + c * 64 + 32, dpb);
       if (!mbar_wait(&bar[kKbPFull0 + s], (i >> 1) & 1, ctx, 51)) { ok = false; break; }
       __syncwarp();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kKbDPEmpty]);
+      if (lane == 0) mbar_arrive(&bar[kKbDPEmpty0 + b]);
       const uint8_t* pbox = smem + Cfg::kOffP + s * Cfg::kPT + c * kBoxBytes;
       uint4 ds[8];
 #pragma unroll
