@@ -501,31 +501,42 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 }
 
 // =============================================================== dkv_kernel
-// Shared memory (D = 128): V_j 32 KB, P_ij x2 64 KB, dS 32 KB, dO_i x2 64 KB,
-// Q_i 32 KB = 224 KB. TMEM: two dP buffers [0,256) (lane = query row, column
-// = key), dV [256,256+D) and dK [256+D,256+2D) (lane = key row, column = d).
+// One CTA per (128-row key tile j, head), walking the query tiles i. The
+// transposed products keep the key index on the TMEM lanes:
+//   dP_ij^T = V_j dO_i^T             (A = V_j, B = dO_i, both K-major over d)
+//   dS_ij^T = P_ij^T (dP_ij^T - D_i) (dS warps; written back into TMEM, 16-bit)
+//   dV_j  += P_ij^T dO_i             (A = P^T, B = dO_i, both MN-major)
+//   dK_j  += dS_ij^T Q_i             (A = dS^T from TMEM, B = Q_i MN-major)
+// so dS never touches shared memory. The dS warps read P^T as 8x8 transposed
+// blocks (ldmatrix.trans) that line up element for element with the
+// .16x256b TMEM fragments of dP^T, and store the packed dS^T pairs with
+// .16x128b, which is the TS operand layout (lane = key, two queries per
+// 32-bit column).
 //
-// Warp roles (12 warps): 0 TMA for V_j and the P stream; 1 MMA issuer for
-// dP (and TMEM owner); 2 TMA for dO_i and Q_i; 3 MMA issuer for dV and dK;
-// 4-11 dS warps (TMEM lane quarter = warp % 4, key half = (warp - 4) / 4),
+// Shared memory (D = 128): V_j 32 KB, P_ij x2 64 KB, dO_i x2 64 KB, Q_i x2
+// 64 KB = 224 KB. TMEM: two dP^T/dS^T buffers [0,256) (lane = key, column =
+// query), dV [256,256+D), dK [256+D,256+2D) (lane = key, column = d).
+//
+// Warp roles (12 warps): 0 TMA for V_j and the P stream; 1 MMA issuer for dP^T
+// (and TMEM owner); 2 TMA for dO_i and Q_i; 3 MMA issuer for dV and dK;
+// 4-11 dS warps (TMEM lane quarter = warp % 4, query half = (warp - 4) / 4),
 // which also write dK_j, dV_j.
 template <int D>
 struct DkvCfg {
   static constexpr int kMD = (D / kBoxCols) * kBoxBytes;
   static constexpr int kPT = 2 * kBoxBytes;
   static constexpr int kOffV = 0;
-  static constexpr int kOffP = kOffV + kMD;  // two stages
-  static constexpr int kOffS = kOffP + 2 * kPT;
-  static constexpr int kOffdO = kOffS + kPT;  // two stages
-  static constexpr int kOffQ = kOffdO + 2 * kMD;
-  static constexpr int kTileBytes = kOffQ + kMD;
+  static constexpr int kOffP = kOffV + kMD;       // two slots
+  static constexpr int kOffdO = kOffP + 2 * kPT;  // two slots
+  static constexpr int kOffQ = kOffdO + 2 * kMD;  // two slots
+  static constexpr int kTileBytes = kOffQ + 2 * kMD;
   static constexpr int kBarBytes = 256;
   static constexpr int kSmemBytes = kTileBytes + kBarBytes + 1024;
   static constexpr int kDSWarps = 8;
   static constexpr int kFirstDSWarp = 4;
   static constexpr int kThreads = 32 * (kFirstDSWarp + kDSWarps);
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kColdP = 0;  // + 128 * buffer (two dP buffers)
+  static constexpr uint32_t kColX = 0;  // + 128 * buffer
   static constexpr uint32_t kColdV = 256;
   static constexpr uint32_t kColdK = 256 + D;
   static_assert(kColdK + D <= kTmemCols, "TMEM budget");
@@ -534,21 +545,21 @@ struct DkvCfg {
 
 enum DkvBar : int {
   kKbV = 0,
-  kKbPFull0 = 1,
-  kKbPEmpty0 = 3,
-  kKbDOFull0 = 5,
-  kKbDOEmpty0 = 7,
-  kKbQFull = 9,
-  kKbQEmpty = 10,
-  kKbDPFull0 = 11,   // + dP buffer (2)
-  kKbDPEmpty0 = 13,  // + dP buffer
-  kKbDSFull = 15,
-  kKbDSEmpty = 16,
-  kKbAcc = 17,
-  kKbDrain = 18,
-  kKbDrain2 = 19,
-  kNumDkvBars = 20,
+  kKbPFull0 = 1,    // + slot (2)
+  kKbPEmpty0 = 3,   // + slot: dV commit + 8 dS warps
+  kKbDOFull0 = 5,   // + slot
+  kKbDOEmpty0 = 7,  // + slot: dP^T commit + dV commit
+  kKbQFull0 = 9,    // + slot
+  kKbQEmpty0 = 11,  // + slot
+  kKbXFull0 = 13,   // + TMEM buffer: dP^T_i computed
+  kKbEFull0 = 15,   // + TMEM buffer: dS^T_i written (8 dS warps)
+  kKbXFree0 = 17,   // + TMEM buffer: dK_i has read dS^T_i
+  kKbAcc = 19,
+  kKbDrain = 20,
+  kKbDrain2 = 21,
+  kNumDkvBars = 22,
 };
+static_assert(kNumDkvBars * 8 + 8 <= 256, "dkv barrier area");
 
 template <typename T, int D>
 __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
@@ -577,16 +588,13 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       mbar_init(&bar[kKbPFull0 + s], 1);
       mbar_init(&bar[kKbPEmpty0 + s], 1 + kEpi);
       mbar_init(&bar[kKbDOFull0 + s], 1);
-      mbar_init(&bar[kKbDOEmpty0 + s], 2);  // read by dP_i and dV_i (two issuers)
+      mbar_init(&bar[kKbDOEmpty0 + s], 2);
+      mbar_init(&bar[kKbQFull0 + s], 1);
+      mbar_init(&bar[kKbQEmpty0 + s], 1);
+      mbar_init(&bar[kKbXFull0 + s], 1);
+      mbar_init(&bar[kKbEFull0 + s], kEpi);
+      mbar_init(&bar[kKbXFree0 + s], 1);
     }
-    mbar_init(&bar[kKbQFull], 1);
-    mbar_init(&bar[kKbQEmpty], 1);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&bar[kKbDPFull0 + b], 1);
-      mbar_init(&bar[kKbDPEmpty0 + b], kEpi);
-    }
-    mbar_init(&bar[kKbDSFull], kEpi);
-    mbar_init(&bar[kKbDSEmpty], 1);
     mbar_init(&bar[kKbAcc], 1);
     mbar_init(&bar[kKbDrain], 1);
     mbar_init(&bar[kKbDrain2], 1);
@@ -604,7 +612,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
   WaitCtx ctx{abort_flag, timeout_ns};
 
   if (warp == 0) {
-    // ---- TMA producer: V_j once, then the P stream (2 stages).
+    // ---- TMA producer: V_j once, then the P stream (2 slots).
     if (lane == 0) {
       tma_prefetch_desc(&tm_V);
       tma_prefetch_desc(&tm_P);
@@ -614,7 +622,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
 #pragma unroll
       for (int b = 0; b < D / kBoxCols; ++b)
         tma_load_3d(smem + Cfg::kOffV + b * kBoxBytes, &tm_V, &bar[kKbV], b * kBoxCols, n0, h, pol_v);
-      constexpr int kAhead = 4;  // P tiles pulled into L2 ahead of the 2-stage ring
+      constexpr int kAhead = 4;  // P tiles pulled into L2 ahead of the 2-slot ring
       for (int i = 0; i < kAhead && i < mt; ++i) {
         tma_prefetch_l2_3d(&tm_P, n0, i * kTile, h);
         tma_prefetch_l2_3d(&tm_P, n0 + kBoxCols, i * kTile, h);
@@ -641,10 +649,10 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       }
     }
   } else if (warp == 2) {
-    // ---- TMA producer for the L2-resident operands: dO_i (2 slots) and Q_i
-    // (1 slot). Polls both "empty" barriers without blocking and issues
-    // whichever load can go; tiles are prefetched into L2 kL2Ahead query
-    // tiles ahead (every key-tile CTA of the head reads them).
+    // ---- TMA producer for the L2-resident operands dO_i and Q_i (two slots
+    // each; every key-tile CTA of the head reads them). Polls both "empty"
+    // barriers without blocking and issues whichever load can go; tiles are
+    // prefetched into L2 kL2Ahead query tiles ahead.
     if (lane == 0) {
       constexpr int kL2Ahead = 3;
       tma_prefetch_desc(&tm_dO);
@@ -660,28 +668,26 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       bool failed = false;
       while ((next_do < mt || next_q < mt) && !failed) {
         bool progressed = false;
-        if (next_do < mt) {
+        if (next_do < mt && (next_do < 2 || mbar_poll(&bar[kKbDOEmpty0 + (next_do & 1)], ((next_do >> 1) - 1) & 1))) {
           const int s = next_do & 1;
-          const int u = next_do >> 1;
-          if (u == 0 || mbar_poll(&bar[kKbDOEmpty0 + s], (u - 1) & 1)) {
-            mbar_arrive_expect_tx(&bar[kKbDOFull0 + s], Cfg::kMD);
-#pragma unroll
-            for (int b = 0; b < D / kBoxCols; ++b)
-              tma_load_3d(smem + Cfg::kOffdO + s * Cfg::kMD + b * kBoxBytes, &tm_dO, &bar[kKbDOFull0 + s],
-                          b * kBoxCols, next_do * kTile, h, pol);
-            if (next_do + kL2Ahead < mt)
-              for (int b = 0; b < D / kBoxCols; ++b)
-                tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, (next_do + kL2Ahead) * kTile, h);
-            ++next_do;
-            progressed = true;
-          }
-        }
-        if (next_q < mt && (next_q == 0 || mbar_poll(&bar[kKbQEmpty], (next_q - 1) & 1))) {
-          mbar_arrive_expect_tx(&bar[kKbQFull], Cfg::kMD);
+          mbar_arrive_expect_tx(&bar[kKbDOFull0 + s], Cfg::kMD);
 #pragma unroll
           for (int b = 0; b < D / kBoxCols; ++b)
-            tma_load_3d(smem + Cfg::kOffQ + b * kBoxBytes, &tm_Q, &bar[kKbQFull], b * kBoxCols,
-                        next_q * kTile, h, pol);
+            tma_load_3d(smem + Cfg::kOffdO + s * Cfg::kMD + b * kBoxBytes, &tm_dO, &bar[kKbDOFull0 + s],
+                        b * kBoxCols, next_do * kTile, h, pol);
+          if (next_do + kL2Ahead < mt)
+            for (int b = 0; b < D / kBoxCols; ++b)
+              tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, (next_do + kL2Ahead) * kTile, h);
+          ++next_do;
+          progressed = true;
+        }
+        if (next_q < mt && (next_q < 2 || mbar_poll(&bar[kKbQEmpty0 + (next_q & 1)], ((next_q >> 1) - 1) & 1))) {
+          const int s = next_q & 1;
+          mbar_arrive_expect_tx(&bar[kKbQFull0 + s], Cfg::kMD);
+#pragma unroll
+          for (int b = 0; b < D / kBoxCols; ++b)
+            tma_load_3d(smem + Cfg::kOffQ + s * Cfg::kMD + b * kBoxBytes, &tm_Q, &bar[kKbQFull0 + s],
+                        b * kBoxCols, next_q * kTile, h, pol);
           if (next_q + kL2Ahead < mt)
             for (int b = 0; b < D / kBoxCols; ++b)
               tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, (next_q + kL2Ahead) * kTile, h);
@@ -701,39 +707,38 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       if (*abort_flag) {
         for (int i = (next_do > 2 ? next_do - 2 : 0); i < next_do; ++i)
           mbar_wait_drain(&bar[kKbDOFull0 + (i & 1)], (i >> 1) & 1, timeout_ns);
-        if (next_q > 0) mbar_wait_drain(&bar[kKbQFull], (next_q - 1) & 1, timeout_ns);
+        for (int i = (next_q > 2 ? next_q - 2 : 0); i < next_q; ++i)
+          mbar_wait_drain(&bar[kKbQFull0 + (i & 1)], (i >> 1) & 1, timeout_ns);
       }
     }
   } else if (warp == 1 || warp == 3) {
     // ---- Two MMA issuers (one keeps the tensor pipe fed while the other
-    // waits). Warp 1: dP_i = dO_i V_j^T. Warp 3: dV_j += P_ij^T dO_i and
-    // dK_j += dS_ij^T Q_i in the order dV_0 dV_1 dK_0 dV_2 dK_1 ..., so the
-    // dS epilogue of tile i overlaps dV_{i+1}.
+    // waits). Warp 1: dP^T_i into TMEM buffer i % 2. Warp 3: dV_j += P^T dO_i
+    // and dK_j += dS^T Q_i in the order dV_0 dV_1 dK_0 dV_2 dK_1 ..., so the
+    // dS warps' work on tile i overlaps dV_{i+1}.
     if (lane == 0) {
       constexpr bool kB = Elem<T>::kBF16;
       constexpr uint32_t id_dP = make_idesc_f16<kB>(kTile, kTile, false, false);
-      constexpr uint32_t id_dVK = make_idesc_f16<kB>(kTile, D, true, true);
+      constexpr uint32_t id_dV = make_idesc_f16<kB>(kTile, D, true, true);
+      constexpr uint32_t id_dK = make_idesc_f16<kB>(kTile, D, false, true);
       const uint32_t sV = smem_u32(smem + Cfg::kOffV);
-      const uint32_t sS = smem_u32(smem + Cfg::kOffS);
-      const uint32_t sQ = smem_u32(smem + Cfg::kOffQ);
       bool ok = true;
       if (warp == 1) {
         ok = mbar_wait(&bar[kKbV], 0, ctx, 45);
         for (int i = 0; i < mt && ok; ++i) {
           const int s = i & 1;
           const uint32_t sdO = smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD);
-          // dP = dO_i V_j^T : A = dO_i (K-major over d), B = V_j (K-major over d).
           if (!mbar_wait(&bar[kKbDOFull0 + s], (i >> 1) & 1, ctx, 40)) { ok = false; break; }
-          // dP buffer b = i % 2 is free once the dS warps have read dP_{i-2}
-          if (i >= 2 && !mbar_wait(&bar[kKbDPEmpty0 + (i & 1)], ((i >> 1) - 1) & 1, ctx, 41)) { ok = false; break; }
+          // buffer i % 2 is free once dK_{i-2} has read dS^T_{i-2} from it
+          if (i >= 2 && !mbar_wait(&bar[kKbXFree0 + s], ((i >> 1) - 1) & 1, ctx, 41)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
             const uint32_t off = (k >> 2) * kBoxBytes + (k & 3) * 32;
-            umma_f16_ss(tmem + Cfg::kColdP + 128 * (i & 1), make_sw128_desc(sdO + off, 16, 1024),
-                        make_sw128_desc(sV + off, 16, 1024), id_dP, k > 0 ? 1u : 0u);
+            umma_f16_ss(tmem + Cfg::kColX + 128 * s, make_sw128_desc(sV + off, 16, 1024),
+                        make_sw128_desc(sdO + off, 16, 1024), id_dP, k > 0 ? 1u : 0u);
           }
-          umma_commit(&bar[kKbDPFull0 + (i & 1)]);
+          umma_commit(&bar[kKbXFull0 + s]);
           umma_commit(&bar[kKbDOEmpty0 + s]);
         }
         if (!ok) {
@@ -752,24 +757,28 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
 #pragma unroll
           for (int k = 0; k < kTile / 16; ++k) {
             umma_f16_ss(tmem + Cfg::kColdV, make_sw128_desc(sP + k * 2048, kBoxBytes, 1024),
-                        make_sw128_desc(sdO + k * 2048, kBoxBytes, 1024), id_dVK, (i > 0 || k > 0) ? 1u : 0u);
+                        make_sw128_desc(sdO + k * 2048, kBoxBytes, 1024), id_dV, (i > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&bar[kKbDOEmpty0 + s]);
           umma_commit(&bar[kKbPEmpty0 + s]);
           return true;
         };
         auto issue_dK = [&](int i) -> bool {
-          // dK += dS^T Q_i : A = dS^T (MN-major, M = key), B = Q_i (MN-major, N = d).
-          if (!mbar_wait(&bar[kKbQFull], i & 1, ctx, 43)) return false;
-          if (!mbar_wait(&bar[kKbDSFull], i & 1, ctx, 44)) return false;
+          const int s = i & 1;
+          const uint32_t sQ = smem_u32(smem + Cfg::kOffQ + s * Cfg::kMD);
+          // dK += dS^T Q_i : A = dS^T from TMEM buffer s (16 queries = 8
+          // packed columns per step), B = Q_i (MN-major, N = d).
+          if (!mbar_wait(&bar[kKbQFull0 + s], (i >> 1) & 1, ctx, 43)) return false;
+          if (!mbar_wait(&bar[kKbEFull0 + s], (i >> 1) & 1, ctx, 44)) return false;
           tc_fence_after();
+          const uint32_t tS = tmem + Cfg::kColX + 128 * s;
 #pragma unroll
           for (int k = 0; k < kTile / 16; ++k) {
-            umma_f16_ss(tmem + Cfg::kColdK, make_sw128_desc(sS + k * 2048, kBoxBytes, 1024),
-                        make_sw128_desc(sQ + k * 2048, kBoxBytes, 1024), id_dVK, (i > 0 || k > 0) ? 1u : 0u);
+            umma_f16_ts(tmem + Cfg::kColdK, tS + (k >> 2) * 64 + (k & 3) * 8,
+                        make_sw128_desc(sQ + k * 2048, kBoxBytes, 1024), id_dK, (i > 0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&bar[kKbQEmpty]);
-          umma_commit(&bar[kKbDSEmpty]);
+          umma_commit(&bar[kKbQEmpty0 + s]);
+          umma_commit(&bar[kKbXFree0 + s]);
           return true;
         };
         ok = issue_dV(0);
@@ -786,58 +795,85 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       }
     }
   } else if (warp >= Cfg::kFirstDSWarp) {
-    // ---- dS warps.
-    const int q = warp & 3;
+    // ---- dS warps. Warp w owns TMEM lane quarter qq = w % 4 (keys
+    // 32qq..32qq+31 of the tile, as two 16-lane halves) and query half c
+    // (queries 64c..64c+63 of each query tile). In the .16x256b fragment,
+    // thread t holds keys t/4 and 8 + t/4 of a half and queries
+    // 8 blk + 2 (t%4) + {0,1} of each 8-query block blk.
+    const int qq = warp & 3;
     const int c = (warp - Cfg::kFirstDSWarp) >> 2;
-    const int r = q * 32 + lane;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    const uint32_t rsw = static_cast<uint32_t>(r);
+    const uint32_t lq = static_cast<uint32_t>(lane & 3);
     bool ok = true;
     for (int i = 0; i < mt && ok; ++i) {
       const int s = i & 1;
-      const int m = i * kTile + r;
-      const float Dm = (m < M) ? __ldg(Dsum + static_cast<int64_t>(h) * M + m) : 0.f;
-      const int b = i & 1;
-      if (!mbar_wait(&bar[kKbDPFull0 + b], (i >> 1) & 1, ctx, 50)) { ok = false; break; }
-      __syncwarp();
-      tc_fence_after();
-      // Both 32-column halves of this warp's dP segment are loaded before any
-      // other work, then the TMEM buffer is released.
-      uint32_t dpa[32], dpb[32];
-      tmem_load_32(lane_base + Cfg::kColdP + 128 * b + c * 64, dpa);
-      tmem_load_32(lane_base + Cfg::kColdP + 128 * b + c * 64 + 32, dpb);
+      // D for this thread's 16 queries (rows of the query tile past M read 0)
+      float Dv[16];
+      {
+        const int64_t drow = static_cast<int64_t>(h) * M;
+        const int q0 = i * kTile + 64 * c + 2 * static_cast<int>(lq);
+#pragma unroll
+        for (int blk = 0; blk < 8; ++blk) {
+          const int q = q0 + 8 * blk;
+          Dv[2 * blk] = q < M ? __ldg(Dsum + drow + q) : 0.f;
+          Dv[2 * blk + 1] = q + 1 < M ? __ldg(Dsum + drow + q + 1) : 0.f;
+        }
+      }
+      if (!mbar_wait(&bar[kKbXFull0 + s], (i >> 1) & 1, ctx, 50)) { ok = false; break; }
       if (!mbar_wait(&bar[kKbPFull0 + s], (i >> 1) & 1, ctx, 51)) { ok = false; break; }
       __syncwarp();
+      tc_fence_after();
+      const uint32_t sP = smem_u32(smem + Cfg::kOffP + s * Cfg::kPT);
+      const uint32_t tX = tmem + Cfg::kColX + 128 * s + 64 * c;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t lane_addr = static_cast<uint32_t>(32 * qq + 16 * hh) << 16;
+        uint32_t dp[32];
+        tmem_load_16x256b_x8(tX + lane_addr, dp);
+        // P^T fragments: for query pair p (queries 16p..16p+15 of the half),
+        // matrices (queries +0..7 | +8..15) x (keys +0..7 | +8..15).
+        uint32_t pf[4][4];
+        {
+          const int m = lane >> 3, rr = lane & 7;
+          const int key = 32 * qq + 16 * hh + 8 * (m >> 1);  // key within the tile
+          const uint32_t box = sP + static_cast<uint32_t>(key >> 6) * kBoxBytes;
+          const uint32_t chunk = static_cast<uint32_t>((key & 63) >> 3);
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const uint32_t row = static_cast<uint32_t>(64 * c + 16 * p + rr + 8 * (m & 1));
+            ldmatrix_x4_trans(box + row * 128u + ((chunk ^ (row & 7u)) << 4), pf[p]);
+          }
+        }
+        uint32_t ds[16];
+#pragma unroll
+        for (int blk = 0; blk < 8; ++blk) {
+          const int p = blk >> 1, odd = blk & 1;
+          const float2 dv = make_float2(-Dv[2 * blk], -Dv[2 * blk + 1]);
+          const float2 ptop = Elem<T>::unpack(pf[p][odd]);
+          const float2 pbot = Elem<T>::unpack(pf[p][2 + odd]);
+          const float2 gtop = make_float2(__uint_as_float(dp[4 * blk]), __uint_as_float(dp[4 * blk + 1]));
+          const float2 gbot = make_float2(__uint_as_float(dp[4 * blk + 2]), __uint_as_float(dp[4 * blk + 3]));
+          const float2 stop = mul_f32x2(ptop, add_f32x2(gtop, dv));
+          const float2 sbot = mul_f32x2(pbot, add_f32x2(gbot, dv));
+          ds[2 * blk] = Elem<T>::pack(stop.x, stop.y);
+          ds[2 * blk + 1] = Elem<T>::pack(sbot.x, sbot.y);
+        }
+        // packed dS^T of the half's 64 queries -> first 32 columns of its region
+        tmem_store_16x128b_x8(tX + lane_addr, ds);
+      }
+      tmem_store_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kKbDPEmpty0 + b]);
-      const uint8_t* pbox = smem + Cfg::kOffP + s * Cfg::kPT + c * kBoxBytes;
-      uint4 ds[8];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 pv = *reinterpret_cast<const uint4*>(pbox + sw128_offset(rsw, j));
-        ds[j] = scale_chunk<T>(pv, dpa + 8 * j, Dm);
+      if (lane == 0) {
+        mbar_arrive(&bar[kKbEFull0 + s]);
+        mbar_arrive(&bar[kKbPEmpty0 + s]);
       }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 pv = *reinterpret_cast<const uint4*>(pbox + sw128_offset(rsw, 4 + j));
-        ds[4 + j] = scale_chunk<T>(pv, dpb + 8 * j, Dm);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kKbPEmpty0 + s]);
-      if (i > 0 && !mbar_wait(&bar[kKbDSEmpty], (i - 1) & 1, ctx, 52)) { ok = false; break; }
-      __syncwarp();
-      uint8_t* sbox = smem + Cfg::kOffS + c * kBoxBytes;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(sbox + sw128_offset(rsw, j)) = ds[j];
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kKbDSFull]);
     }
     // final dV_j and dK_j rows (lane = key row) -> 16-bit outputs
     if (ok && mbar_wait(&bar[kKbAcc], 0, ctx, 53)) {
       __syncwarp();
       tc_fence_after();
+      const int r = qq * 32 + lane;
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(qq * 32) << 16);
       const int n = n0 + r;
       constexpr int kHalf = D / 2;
 #pragma unroll

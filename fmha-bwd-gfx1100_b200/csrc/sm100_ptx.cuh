@@ -310,6 +310,41 @@ __device__ __forceinline__ void tmem_store_32(uint32_t taddr, const uint32_t (&r
                : "memory");
 }
 
+// 16 TMEM lanes x 64 fp32 columns, MMA-fragment layout (.16x256b.x8): thread
+// t receives, for column block b = 0..7 (columns 8b..8b+7 from taddr),
+// r[4b], r[4b+1] = lane (t / 4), columns 8b + 2 (t % 4) + {0, 1} and
+// r[4b+2], r[4b+3] = lane 8 + (t / 4), same columns (lanes relative to the
+// lane in taddr, which must lie in the warp's lane quarter). Load and wait in
+// one statement, as tmem_load_32.
+__device__ __forceinline__ void tmem_load_16x256b_x8(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// 16 TMEM lanes x 32 columns (.16x128b.x8): for column block b = 0..7
+// (columns 4b..4b+3), thread t writes r[2b] to lane t / 4 and r[2b+1] to
+// lane 8 + t / 4, column 4b + t % 4. Complete with tmem_store_wait().
+__device__ __forceinline__ void tmem_store_16x128b_x8(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile("tcgen05.st.sync.aligned.16x128b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
+               :
+               : "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+               : "memory");
+}
+
+// Four transposed 8x8 16-bit matrices from shared memory: thread t gives the
+// address of one 16-byte row (matrix t / 8, row t % 8) and receives, for
+// matrix m, the pair (row 2 (t % 4), row 2 (t % 4) + 1) of column t / 4 in
+// r[m] (low half = the first row).
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t saddr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(saddr));
+}
+
 __device__ __forceinline__ void tmem_store_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
