@@ -67,7 +67,7 @@ def load_traffic(key: str):
         with open(TRAFFIC_FILE) as f:
             for line in f:
                 if ":" in line and not line.lstrip().startswith("#"):
-                    k, v = line.split(":", 1)
+                    k, v = line.rsplit(":", 1)
                     if k.strip() == key:
                         return float(v.split()[0])
     except OSError:
@@ -225,9 +225,9 @@ def main() -> int:
     ap.add_argument("--workload", default="flux")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-rows", type=int, default=0,
-                    help="query rows per head in the CPU baseline sample (0: all M rows, "
-                         "i.e. whole heads, about 10-15 s on 16 host cores at FLUX)")
+    ap.add_argument("--cpu-rows", type=int, default=2048,
+                    help="query rows per head in the CPU baseline sample (0: all M rows); "
+                         "2048 rows of 16 FLUX heads take about 15 s on 16 host cores")
     ap.add_argument("--cpu-rows-per-step", type=int, default=0,
                     help="query rows per head per step of the reference arm "
                          "(0: sized so the run takes about two minutes)")

@@ -714,8 +714,8 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
   } else if (warp == 1 || warp == 3) {
     // ---- Two MMA issuers (one keeps the tensor pipe fed while the other
     // waits). Warp 1: dP^T_i into TMEM buffer i % 2. Warp 3: dV_j += P^T dO_i
-    // and dK_j += dS^T Q_i in the order dV_0 dV_1 dK_0 dV_2 dK_1 ..., so the
-    // dS warps' work on tile i overlaps dV_{i+1}.
+    // and dK_j += dS^T Q_i in the order dV_0 dK_0 dV_1 dK_1 ...: dK_i goes
+    // first because buffer i % 2 (and so dP^T_{i+2}) waits for it.
     if (lane == 0) {
       constexpr bool kB = Elem<T>::kBF16;
       constexpr uint32_t id_dP = make_idesc_f16<kB>(kTile, kTile, false, false);
@@ -783,8 +783,8 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         };
         ok = issue_dV(0);
         for (int i = 0; i < mt && ok; ++i) {
-          if (i + 1 < mt && !issue_dV(i + 1)) { ok = false; break; }
           if (!issue_dK(i)) { ok = false; break; }
+          if (i + 1 < mt && !issue_dV(i + 1)) { ok = false; break; }
         }
         if (ok) {
           umma_commit(&bar[kKbAcc]);
