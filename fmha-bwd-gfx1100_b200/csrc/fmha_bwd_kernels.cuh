@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 #pragma unroll
       for (int x = 0; x < 8; ++x) pv[x] = *reinterpret_cast<const uint4*>(pbox + sw128_offset(rsw, x));
       // sum_n P dP (and, on the first key tile, sum_n P for the shift)
-      float sp = 0.f, spdp = 0.f;
+      float spdp = 0.f;
 #pragma unroll
       for (int x = 0; x < 8; ++x) {
         const uint32_t pw[4] = {pv[x].x, pv[x].y, pv[x].z, pv[x].w};
@@ -436,12 +436,21 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
           const float2 p = Elem<T>::unpack(pw[t]);
           spdp = fmaf(p.x, __uint_as_float(dp[2 * t]), spdp);
           spdp = fmaf(p.y, __uint_as_float(dp[2 * t + 1]), spdp);
-          sp += p.x + p.y;
         }
       }
       Dacc += spdp;
       if (j == 0) {
         // shift c_i = P-weighted mean of dP over key tile 0 (both halves)
+        float sp = 0.f;
+#pragma unroll
+        for (int x = 0; x < 8; ++x) {
+          const uint32_t pw[4] = {pv[x].x, pv[x].y, pv[x].z, pv[x].w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float2 p = Elem<T>::unpack(pw[t]);
+            sp += p.x + p.y;
+          }
+        }
         float sp_o = 0.f, spdp_o = 0.f;
         if (!swap(sp, sp_o, true) || !swap(spdp, spdp_o, true)) { ok = false; break; }
         const float sp_all = sp + sp_o;

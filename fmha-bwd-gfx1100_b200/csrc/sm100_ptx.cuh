@@ -518,6 +518,15 @@ __device__ __forceinline__ float2 mul_f32x2(float2 a, float2 b) {
   return c;
 }
 
+__device__ __forceinline__ float2 fma_f32x2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)),
+        "l"(reinterpret_cast<const uint64_t&>(c)));
+  return d;
+}
+
 // ------------------------------------------------------------ misc helpers
 __device__ __forceinline__ void red_add_f32(float* gaddr, float v) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(gaddr), "f"(v) : "memory");
