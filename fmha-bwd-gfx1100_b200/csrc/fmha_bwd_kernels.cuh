@@ -176,11 +176,13 @@ enum DqBar : int {
   kQbXFull0 = 19,   // + buffer (2)
   kQbEFull0 = 21,   // + buffer
   kQbXFree0 = 23,   // + buffer
-  kQbAB = 25,
+  kQbAB = 25,       // A and B of an item complete
   kQbDrain = 26,
   kQbXch0 = 27,     // + lane quarter (4): the two warps of a quarter swap values
   kQbDrain2 = 31,   // drain of the second MMA issuer
-  kNumDqBars = 32,
+  kQbDOEmpty = 32,  // the dP MMAs of an item are done with dO_i
+  kQbAccEmpty = 33, // the dS warps have read an item's A and B (8 warps)
+  kNumDqBars = 34,
 };
 static_assert(kNumDqBars * 8 + 8 <= 512, "dq barrier area");
 
@@ -188,7 +190,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
     dq_kernel(const __grid_constant__ CUtensorMap tm_P, const __grid_constant__ CUtensorMap tm_V,
               const __grid_constant__ CUtensorMap tm_K, const __grid_constant__ CUtensorMap tm_dO,
-              T* __restrict__ dQ, float* __restrict__ Dsum, int M, int N,
+              T* __restrict__ dQ, float* __restrict__ Dsum, int M, int N, int H,
               KernelStatus* status, uint64_t timeout_ns) {
   using Cfg = DqCfg<D>;
   constexpr int SV = Cfg::kSV, SK = Cfg::kSK, SP = Cfg::kSP;
@@ -202,12 +204,13 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kTile;
-  const int h = blockIdx.y;
+  const int mt = (M + kTile - 1) / kTile;
   const int nt = (N + kTile - 1) / kTile;
+  const int tiles = mt * H;  // work items (query tile, head), head-major
 
   if (threadIdx.x == 0) {
     mbar_init(&bar[kQbDO], 1);
+    mbar_init(&bar[kQbDOEmpty], 1);
     for (int s = 0; s < SV; ++s) {
       mbar_init(&bar[kQbVFull0 + s], 1);
       mbar_init(&bar[kQbVEmpty0 + s], 1);
@@ -226,6 +229,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       mbar_init(&bar[kQbXFree0 + b], 1);
     }
     mbar_init(&bar[kQbAB], 1);
+    mbar_init(&bar[kQbAccEmpty], Cfg::kEpiWarps);
     mbar_init(&bar[kQbDrain], 1);
     mbar_init(&bar[kQbDrain2], 1);
     for (int q = 0; q < 4; ++q) mbar_init(&bar[kQbXch0 + q], 2);
@@ -242,9 +246,12 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   WaitCtx ctx{abort_flag, timeout_ns};
 
+  // Every role walks the same work items: t = blockIdx.x, + gridDim.x, ...
+  // Shared-memory rings, TMEM buffers and their barrier phases continue
+  // across items (global step counter g over (item, key tile)).
   if (warp == 0) {
-    // ---- TMA producer: dO_i once, then V_j, P_ij, K_j in the order the
-    // tensor core needs them, each into the next slot of its own ring.
+    // ---- TMA producer: per item dO_i (once the previous item's dP MMAs are
+    // done), then V_j, P_ij, K_j in the order the tensor core needs them.
     if (lane == 0) {
       tma_prefetch_desc(&tm_P);
       tma_prefetch_desc(&tm_V);
@@ -252,54 +259,59 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       tma_prefetch_desc(&tm_dO);
       const uint64_t pol_p = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();
-      mbar_arrive_expect_tx(&bar[kQbDO], Cfg::kMD);
+      constexpr int kAhead = 4;  // P tiles pulled into L2 ahead of the ring
+      int g = 0, nV = 0, nP = 0, nK = 0, nD = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int h = t / mt;
+        const int m0 = (t - h * mt) * kTile;
+        auto prefetch = [&](int j) {
+          tma_prefetch_l2_3d(&tm_P, j * kTile, m0, h);
+          tma_prefetch_l2_3d(&tm_P, j * kTile + kBoxCols, m0, h);
+        };
+        for (int j = 0; j < kAhead && j < nt; ++j) prefetch(j);
+        if (nD > 0 && !mbar_wait(&bar[kQbDOEmpty], (nD - 1) & 1, ctx, 4)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bar[kQbDO], Cfg::kMD);
 #pragma unroll
-      for (int b = 0; b < D / kBoxCols; ++b)
-        tma_load_3d(smem + Cfg::kOffdO + b * kBoxBytes, &tm_dO, &bar[kQbDO], b * kBoxCols, m0, h, pol_kv);
-      // P streams from HBM: pull it into L2 a few key tiles ahead so the
-      // shared-memory load that follows once a slot frees is an L2 hit.
-      constexpr int kAhead = 4;
-      auto prefetch = [&](int j) {
-        tma_prefetch_l2_3d(&tm_P, j * kTile, m0, h);
-        tma_prefetch_l2_3d(&tm_P, j * kTile + kBoxCols, m0, h);
-      };
-      for (int j = 0; j < kAhead && j < nt; ++j) prefetch(j);
-      int nV = 0, nP = 0, nK = 0;  // loads issued per ring
-      for (int j = 0; j < nt; ++j) {
-        if (j + kAhead < nt) prefetch(j + kAhead);
-        if (j >= SV && !mbar_wait(&bar[kQbVEmpty0 + j % SV], ((j / SV) - 1) & 1, ctx, 1)) break;
-        {
-          uint64_t* fb = &bar[kQbVFull0 + j % SV];
-          uint8_t* dst = smem + Cfg::kOffV + (j % SV) * Cfg::kMD;
-          mbar_arrive_expect_tx(fb, Cfg::kMD);
+        for (int b = 0; b < D / kBoxCols; ++b)
+          tma_load_3d(smem + Cfg::kOffdO + b * kBoxBytes, &tm_dO, &bar[kQbDO], b * kBoxCols, m0, h, pol_kv);
+        ++nD;
+        for (int j = 0; j < nt; ++j, ++g) {
+          if (j + kAhead < nt) prefetch(j + kAhead);
+          if (g >= SV && !mbar_wait(&bar[kQbVEmpty0 + g % SV], ((g / SV) - 1) & 1, ctx, 1)) { ok = false; break; }
+          {
+            uint64_t* fb = &bar[kQbVFull0 + g % SV];
+            uint8_t* dst = smem + Cfg::kOffV + (g % SV) * Cfg::kMD;
+            mbar_arrive_expect_tx(fb, Cfg::kMD);
 #pragma unroll
-          for (int b = 0; b < D / kBoxCols; ++b)
-            tma_load_3d(dst + b * kBoxBytes, &tm_V, fb, b * kBoxCols, j * kTile, h, pol_kv);
-          ++nV;
-        }
-        if (j >= SP && !mbar_wait(&bar[kQbPEmpty0 + j % SP], ((j / SP) - 1) & 1, ctx, 2)) break;
-        {
-          uint64_t* fb = &bar[kQbPFull0 + j % SP];
-          uint8_t* dst = smem + Cfg::kOffP + (j % SP) * Cfg::kPT;
-          mbar_arrive_expect_tx(fb, Cfg::kPT);
-          tma_load_3d(dst, &tm_P, fb, j * kTile, m0, h, pol_p);
-          tma_load_3d(dst + kBoxBytes, &tm_P, fb, j * kTile + kBoxCols, m0, h, pol_p);
-          ++nP;
-        }
-        if (j >= SK && !mbar_wait(&bar[kQbKEmpty0 + j % SK], ((j / SK) - 1) & 1, ctx, 3)) break;
-        {
-          uint64_t* fb = &bar[kQbKFull0 + j % SK];
-          uint8_t* dst = smem + Cfg::kOffK + (j % SK) * Cfg::kMD;
-          mbar_arrive_expect_tx(fb, Cfg::kMD);
+            for (int b = 0; b < D / kBoxCols; ++b)
+              tma_load_3d(dst + b * kBoxBytes, &tm_V, fb, b * kBoxCols, j * kTile, h, pol_kv);
+            ++nV;
+          }
+          if (g >= SP && !mbar_wait(&bar[kQbPEmpty0 + g % SP], ((g / SP) - 1) & 1, ctx, 2)) { ok = false; break; }
+          {
+            uint64_t* fb = &bar[kQbPFull0 + g % SP];
+            uint8_t* dst = smem + Cfg::kOffP + (g % SP) * Cfg::kPT;
+            mbar_arrive_expect_tx(fb, Cfg::kPT);
+            tma_load_3d(dst, &tm_P, fb, j * kTile, m0, h, pol_p);
+            tma_load_3d(dst + kBoxBytes, &tm_P, fb, j * kTile + kBoxCols, m0, h, pol_p);
+            ++nP;
+          }
+          if (g >= SK && !mbar_wait(&bar[kQbKEmpty0 + g % SK], ((g / SK) - 1) & 1, ctx, 3)) { ok = false; break; }
+          {
+            uint64_t* fb = &bar[kQbKFull0 + g % SK];
+            uint8_t* dst = smem + Cfg::kOffK + (g % SK) * Cfg::kMD;
+            mbar_arrive_expect_tx(fb, Cfg::kMD);
 #pragma unroll
-          for (int b = 0; b < D / kBoxCols; ++b)
-            tma_load_3d(dst + b * kBoxBytes, &tm_K, fb, b * kBoxCols, j * kTile, h, pol_kv);
-          ++nK;
+            for (int b = 0; b < D / kBoxCols; ++b)
+              tma_load_3d(dst + b * kBoxBytes, &tm_K, fb, b * kBoxCols, j * kTile, h, pol_kv);
+            ++nK;
+          }
         }
       }
       if (*abort_flag) {
         // let every copy still in flight land before the CTA exits
-        mbar_wait_drain(&bar[kQbDO], 0, timeout_ns);
+        if (nD > 0) mbar_wait_drain(&bar[kQbDO], (nD - 1) & 1, timeout_ns);
         for (int j = (nV > SV ? nV - SV : 0); j < nV; ++j)
           mbar_wait_drain(&bar[kQbVFull0 + j % SV], (j / SV) & 1, timeout_ns);
         for (int j = (nP > SP ? nP - SP : 0); j < nP; ++j)
@@ -312,8 +324,9 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
     // ---- Two MMA issuers. The tensor pipe accepts only about one
     // instruction ahead of the one executing, so a single issuing thread
     // leaves it idle at every wait; with two, one keeps it fed while the
-    // other waits. Warp 1: dP_j = dO_i V_j^T into X_(j%2). Warp kAbWarp:
-    // B_j += P_ij K_j, then A_j += E_ij K_j (E from TMEM).
+    // other waits. Warp 1: dP_j = dO_i V_j^T into X_(g%2). Warp kAbWarp:
+    // B_j += P_ij K_j, then A_j += E_ij K_j (E from TMEM); it starts an item
+    // once the dS warps have read the previous item's A and B.
     if (lane == 0) {
       constexpr bool kB = Elem<T>::kBF16;
       // dP = dO_i V_j^T: A = dO_i (K-major over d), B = V_j (K-major over d)
@@ -325,55 +338,61 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       const uint32_t sK0 = smem_u32(smem + Cfg::kOffK);
       const uint32_t sP0 = smem_u32(smem + Cfg::kOffP);
       bool ok = true;
+      int g = 0, tc = 0;
       if (warp == 1) {
-        ok = mbar_wait(&bar[kQbDO], 0, ctx, 13);
-        for (int j = 0; j < nt && ok; ++j) {
-          if (!mbar_wait(&bar[kQbVFull0 + j % SV], (j / SV) & 1, ctx, 10)) { ok = false; break; }
-          if (j >= 2 && !mbar_wait(&bar[kQbXFree0 + (j & 1)], ((j >> 1) - 1) & 1, ctx, 11)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t sV = sV0 + (j % SV) * Cfg::kMD;
-          const uint32_t tX = tmem + Cfg::kColX + 128 * (j & 1);
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+          if (!mbar_wait(&bar[kQbDO], tc & 1, ctx, 13)) { ok = false; break; }
+          for (int j = 0; j < nt; ++j, ++g) {
+            if (!mbar_wait(&bar[kQbVFull0 + g % SV], (g / SV) & 1, ctx, 10)) { ok = false; break; }
+            if (g >= 2 && !mbar_wait(&bar[kQbXFree0 + (g & 1)], ((g >> 1) - 1) & 1, ctx, 11)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sV = sV0 + (g % SV) * Cfg::kMD;
+            const uint32_t tX = tmem + Cfg::kColX + 128 * (g & 1);
 #pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint32_t off = (k >> 2) * kBoxBytes + (k & 3) * 32;
-            umma_f16_ss(tX, make_sw128_desc(sdO + off, 16, 1024), make_sw128_desc(sV + off, 16, 1024), id_dP,
-                        k > 0 ? 1u : 0u);
+            for (int k = 0; k < D / 16; ++k) {
+              const uint32_t off = (k >> 2) * kBoxBytes + (k & 3) * 32;
+              umma_f16_ss(tX, make_sw128_desc(sdO + off, 16, 1024), make_sw128_desc(sV + off, 16, 1024), id_dP,
+                          k > 0 ? 1u : 0u);
+            }
+            umma_commit(&bar[kQbXFull0 + (g & 1)]);
+            umma_commit(&bar[kQbVEmpty0 + g % SV]);  // V_j consumed
           }
-          umma_commit(&bar[kQbXFull0 + (j & 1)]);
-          umma_commit(&bar[kQbVEmpty0 + j % SV]);  // V_j consumed
+          if (ok) umma_commit(&bar[kQbDOEmpty]);  // dO_i consumed
         }
         if (!ok) {
           umma_commit(&bar[kQbDrain]);
           mbar_wait_drain(&bar[kQbDrain], 0, timeout_ns);
         }
       } else {
-        for (int j = 0; j < nt && ok; ++j) {
-          if (!mbar_wait(&bar[kQbPFull0 + j % SP], (j / SP) & 1, ctx, 14)) { ok = false; break; }
-          if (!mbar_wait(&bar[kQbKFull0 + j % SK], (j / SK) & 1, ctx, 15)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t sP = sP0 + (j % SP) * Cfg::kPT;
-          const uint32_t sK = sK0 + (j % SK) * Cfg::kMD;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+          if (tc > 0 && !mbar_wait(&bar[kQbAccEmpty], (tc - 1) & 1, ctx, 16)) { ok = false; break; }
+          for (int j = 0; j < nt; ++j, ++g) {
+            if (!mbar_wait(&bar[kQbPFull0 + g % SP], (g / SP) & 1, ctx, 14)) { ok = false; break; }
+            if (!mbar_wait(&bar[kQbKFull0 + g % SK], (g / SK) & 1, ctx, 15)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sP = sP0 + (g % SP) * Cfg::kPT;
+            const uint32_t sK = sK0 + (g % SK) * Cfg::kMD;
 #pragma unroll
-          for (int k = 0; k < kTile / 16; ++k) {
-            umma_f16_ss(tmem + Cfg::kColB, make_sw128_desc(sP + (k >> 2) * kBoxBytes + (k & 3) * 32, 16, 1024),
-                        make_sw128_desc(sK + k * 2048, kBoxBytes, 1024), id_AB, (j > 0 || k > 0) ? 1u : 0u);
-          }
-          umma_commit(&bar[kQbPEmpty0 + j % SP]);  // the tensor core's read of P_ij
-          if (!mbar_wait(&bar[kQbEFull0 + (j & 1)], (j >> 1) & 1, ctx, 12)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t tE = tmem + Cfg::kColX + 128 * (j & 1);
+            for (int k = 0; k < kTile / 16; ++k) {
+              umma_f16_ss(tmem + Cfg::kColB, make_sw128_desc(sP + (k >> 2) * kBoxBytes + (k & 3) * 32, 16, 1024),
+                          make_sw128_desc(sK + k * 2048, kBoxBytes, 1024), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+            }
+            umma_commit(&bar[kQbPEmpty0 + g % SP]);  // the tensor core's read of P_ij
+            if (!mbar_wait(&bar[kQbEFull0 + (g & 1)], (g >> 1) & 1, ctx, 12)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t tE = tmem + Cfg::kColX + 128 * (g & 1);
 #pragma unroll
-          for (int k = 0; k < kTile / 16; ++k) {
-            // E for keys 16k..16k+15 sits in key half (k >> 2): 8 columns per step
-            umma_f16_ts(tmem + Cfg::kColA, tE + (k >> 2) * 64 + (k & 3) * 8,
-                        make_sw128_desc(sK + k * 2048, kBoxBytes, 1024), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < kTile / 16; ++k) {
+              // E for keys 16k..16k+15 sits in key half (k >> 2): 8 columns per step
+              umma_f16_ts(tmem + Cfg::kColA, tE + (k >> 2) * 64 + (k & 3) * 8,
+                          make_sw128_desc(sK + k * 2048, kBoxBytes, 1024), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+            }
+            umma_commit(&bar[kQbKEmpty0 + g % SK]);  // K_j consumed (B_j and A_j)
+            umma_commit(&bar[kQbXFree0 + (g & 1)]);
           }
-          umma_commit(&bar[kQbKEmpty0 + j % SK]);  // K_j consumed (B_j and A_j)
-          umma_commit(&bar[kQbXFree0 + (j & 1)]);
+          if (ok) umma_commit(&bar[kQbAB]);  // A and B of this item complete
         }
-        if (ok) {
-          umma_commit(&bar[kQbAB]);
-        } else {
+        if (!ok) {
           umma_commit(&bar[kQbDrain2]);
           mbar_wait_drain(&bar[kQbDrain2], 0, timeout_ns);
         }
@@ -387,11 +406,8 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
     const int q = warp & 3;
     const int c = (warp - Cfg::kFirstEpiWarp) >> 2;
     const int r = q * 32 + lane;
-    const int m = m0 + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const uint32_t rsw = static_cast<uint32_t>(r);
-    float Dacc = 0.f;   // this half's sum_n P dP over all key tiles
-    float shift = 0.f;  // c_i
     uint32_t xphase = 0;
     // One round: both warps of the quarter have arrived.
     auto xch_round = [&]() -> bool {
@@ -402,85 +418,92 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       __syncwarp();
       return w;
     };
-    // Partner's value for this row; `reuse` adds the round that lets the
-    // partner read before xch is written again.
-    auto swap = [&](float mine, float& other, bool reuse) -> bool {
+    // Partner's value for this row; the second round lets the partner read
+    // before xch is written again.
+    auto swap = [&](float mine, float& other) -> bool {
       xch[c * kTile + r] = mine;
       if (!xch_round()) return false;
       other = xch[(1 - c) * kTile + r];
-      return reuse ? xch_round() : true;
+      return xch_round();
     };
     bool ok = true;
-    for (int j = 0; j < nt && ok; ++j) {
-      const int s = j % SP;
-      const int b = j & 1;
-      if (!mbar_wait(&bar[kQbXFull0 + b], (j >> 1) & 1, ctx, 20)) { ok = false; break; }
-      if (!mbar_wait(&bar[kQbPFull0 + s], (j / SP) & 1, ctx, 21)) { ok = false; break; }
-      __syncwarp();
-      tc_fence_after();
-      uint32_t dpa[32], dpb[32];
-      tmem_load_32(lane_base + Cfg::kColX + 128 * b + 64 * c, dpa);
-      tmem_load_32(lane_base + Cfg::kColX + 128 * b + 64 * c + 32, dpb);
-      const uint8_t* pbox = smem + Cfg::kOffP + s * Cfg::kPT + c * kBoxBytes;
-      uint4 pv[8];
+    int g = 0, tc = 0;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+      const int h = t / mt;
+      const int m = (t - h * mt) * kTile + r;
+      float Dacc = 0.f;   // this half's sum_n P dP over all key tiles
+      float shift = 0.f;  // c_i
+      for (int j = 0; j < nt; ++j, ++g) {
+        const int s = g % SP;
+        const int b = g & 1;
+        if (!mbar_wait(&bar[kQbXFull0 + b], (g >> 1) & 1, ctx, 20)) { ok = false; break; }
+        if (!mbar_wait(&bar[kQbPFull0 + s], (g / SP) & 1, ctx, 21)) { ok = false; break; }
+        __syncwarp();
+        tc_fence_after();
+        uint32_t dpa[32], dpb[32];
+        tmem_load_32(lane_base + Cfg::kColX + 128 * b + 64 * c, dpa);
+        tmem_load_32(lane_base + Cfg::kColX + 128 * b + 64 * c + 32, dpb);
+        const uint8_t* pbox = smem + Cfg::kOffP + s * Cfg::kPT + c * kBoxBytes;
+        uint4 pv[8];
 #pragma unroll
-      for (int x = 0; x < 8; ++x) pv[x] = *reinterpret_cast<const uint4*>(pbox + sw128_offset(rsw, x));
-      // sum_n P dP (and, on the first key tile, sum_n P for the shift)
-      float spdp = 0.f;
-#pragma unroll
-      for (int x = 0; x < 8; ++x) {
-        const uint32_t pw[4] = {pv[x].x, pv[x].y, pv[x].z, pv[x].w};
-        const uint32_t* dp = x < 4 ? dpa + 8 * x : dpb + 8 * (x - 4);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float2 p = Elem<T>::unpack(pw[t]);
-          spdp = fmaf(p.x, __uint_as_float(dp[2 * t]), spdp);
-          spdp = fmaf(p.y, __uint_as_float(dp[2 * t + 1]), spdp);
-        }
-      }
-      Dacc += spdp;
-      if (j == 0) {
-        // shift c_i = P-weighted mean of dP over key tile 0 (both halves)
-        float sp = 0.f;
+        for (int x = 0; x < 8; ++x) pv[x] = *reinterpret_cast<const uint4*>(pbox + sw128_offset(rsw, x));
+        // sum_n P dP over this half tile
+        float spdp = 0.f;
 #pragma unroll
         for (int x = 0; x < 8; ++x) {
           const uint32_t pw[4] = {pv[x].x, pv[x].y, pv[x].z, pv[x].w};
+          const uint32_t* dp = x < 4 ? dpa + 8 * x : dpb + 8 * (x - 4);
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const float2 p = Elem<T>::unpack(pw[t]);
-            sp += p.x + p.y;
+          for (int u = 0; u < 4; ++u) {
+            const float2 p = Elem<T>::unpack(pw[u]);
+            spdp = fmaf(p.x, __uint_as_float(dp[2 * u]), spdp);
+            spdp = fmaf(p.y, __uint_as_float(dp[2 * u + 1]), spdp);
           }
         }
-        float sp_o = 0.f, spdp_o = 0.f;
-        if (!swap(sp, sp_o, true) || !swap(spdp, spdp_o, true)) { ok = false; break; }
-        const float sp_all = sp + sp_o;
-        shift = sp_all > 1e-30f ? (spdp + spdp_o) / sp_all : 0.f;
-      }
-      // E = P (dP - c) in 16-bit, 32 packed columns at X_b + 64c
-      uint32_t e[32];
+        Dacc += spdp;
+        if (j == 0) {
+          // shift c_i = P-weighted mean of dP over key tile 0 (both halves)
+          float sp = 0.f;
 #pragma unroll
-      for (int x = 0; x < 8; ++x) {
-        const uint4 ev = scale_chunk<T>(pv[x], x < 4 ? dpa + 8 * x : dpb + 8 * (x - 4), shift);
-        e[4 * x + 0] = ev.x;
-        e[4 * x + 1] = ev.y;
-        e[4 * x + 2] = ev.z;
-        e[4 * x + 3] = ev.w;
+          for (int x = 0; x < 8; ++x) {
+            const uint32_t pw[4] = {pv[x].x, pv[x].y, pv[x].z, pv[x].w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float2 p = Elem<T>::unpack(pw[u]);
+              sp += p.x + p.y;
+            }
+          }
+          float sp_o = 0.f, spdp_o = 0.f;
+          if (!swap(sp, sp_o) || !swap(spdp, spdp_o)) { ok = false; break; }
+          const float sp_all = sp + sp_o;
+          shift = sp_all > 1e-30f ? (spdp + spdp_o) / sp_all : 0.f;
+        }
+        // E = P (dP - c) in 16-bit, 32 packed columns at X_b + 64c
+        uint32_t e[32];
+#pragma unroll
+        for (int x = 0; x < 8; ++x) {
+          const uint4 ev = scale_chunk<T>(pv[x], x < 4 ? dpa + 8 * x : dpb + 8 * (x - 4), shift);
+          e[4 * x + 0] = ev.x;
+          e[4 * x + 1] = ev.y;
+          e[4 * x + 2] = ev.z;
+          e[4 * x + 3] = ev.w;
+        }
+        tmem_store_32(lane_base + Cfg::kColX + 128 * b + 64 * c, e);
+        tmem_store_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bar[kQbEFull0 + b]);
+          mbar_arrive(&bar[kQbPEmpty0 + s]);
+        }
       }
-      tmem_store_32(lane_base + Cfg::kColX + 128 * b + 64 * c, e);
-      tmem_store_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bar[kQbEFull0 + b]);
-        mbar_arrive(&bar[kQbPEmpty0 + s]);
-      }
-    }
-    // dQ = A - (D - c) B, and D
-    if (ok && mbar_wait(&bar[kQbAB], 0, ctx, 22)) {
+      if (!ok) break;
+      // dQ = A - (D - c) B, and D; then hand A and B back to the issuer
+      if (!mbar_wait(&bar[kQbAB], tc & 1, ctx, 22)) { ok = false; break; }
       __syncwarp();
       tc_fence_after();
       float Dother = 0.f;
-      const bool swapped = swap(Dacc, Dother, false);
+      if (!swap(Dacc, Dother)) { ok = false; break; }
       const float Dfull = Dacc + Dother;
       const float sD = Dfull - shift;
       constexpr int kHalf = D / 2;
@@ -493,10 +516,12 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
         float v[32];
 #pragma unroll
         for (int y = 0; y < 32; ++y) v[y] = fmaf(-sD, __uint_as_float(bb[y]), __uint_as_float(a[y]));
-        if (swapped && m < M) store_row_32<T>(out + 32 * x, v);
+        if (m < M) store_row_32<T>(out + 32 * x, v);
       }
-      if (swapped && c == 0 && m < M) Dsum[static_cast<int64_t>(h) * M + m] = Dfull;
+      if (c == 0 && m < M) Dsum[static_cast<int64_t>(h) * M + m] = Dfull;
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kQbAccEmpty]);
     }
   }
 

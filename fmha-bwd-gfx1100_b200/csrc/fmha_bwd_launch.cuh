@@ -257,18 +257,24 @@ int enqueue_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, co
     if (events && events[k]) cudaEventRecord(events[k], stream);
   };
   const int mt = (M + kTile - 1) / kTile;
-  const dim3 grid_rows(mt, H);
+  int device = 0, sms = 0;
+  cudaGetDevice(&device);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (sms <= 0) sms = 148;
+  // the dQ kernel is persistent: one CTA per SM walks the (query tile, head) items
+  const long long items = static_cast<long long>(mt) * H;
+  const dim3 grid_rows(static_cast<unsigned>(items < sms ? items : sms));
   const dim3 grid_cols((N + kTile - 1) / kTile, H);
   mark(0);
   if (D == 128) {
     dq_kernel<T, 128><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
-        mP, mV, mK, mdO, dQ, dsum, M, N, st, tmo);
+        mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
     mark(1);
     dkv_kernel<T, 128><<<grid_cols, DkvCfg<128>::kThreads, DkvCfg<128>::kSmemBytes, stream>>>(
         mQ, mV, mdO, mP, dsum, dK, dV, M, N, st, tmo);
   } else {
     dq_kernel<T, 64><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
-        mP, mV, mK, mdO, dQ, dsum, M, N, st, tmo);
+        mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
     mark(1);
     dkv_kernel<T, 64><<<grid_cols, DkvCfg<64>::kThreads, DkvCfg<64>::kSmemBytes, stream>>>(
         mQ, mV, mdO, mP, dsum, dK, dV, M, N, st, tmo);
