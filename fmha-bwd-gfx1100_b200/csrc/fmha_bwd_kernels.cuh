@@ -588,10 +588,12 @@ enum DkvBar : int {
   kKbXFull0 = 13,   // + TMEM buffer: dP^T_i computed
   kKbEFull0 = 15,   // + TMEM buffer: dS^T_i written (8 dS warps)
   kKbXFree0 = 17,   // + TMEM buffer: dK_i has read dS^T_i
-  kKbAcc = 19,
+  kKbAcc = 19,       // dV and dK of an item complete
   kKbDrain = 20,
   kKbDrain2 = 21,
-  kNumDkvBars = 22,
+  kKbVEmpty = 22,    // the dP^T MMAs of an item are done with V_j
+  kKbAccEmpty = 23,  // the dS warps have read an item's dV and dK (8 warps)
+  kNumDkvBars = 24,
 };
 static_assert(kNumDkvBars * 8 + 8 <= 256, "dkv barrier area");
 
@@ -600,7 +602,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     dkv_kernel(const __grid_constant__ CUtensorMap tm_Q, const __grid_constant__ CUtensorMap tm_V,
                const __grid_constant__ CUtensorMap tm_dO, const __grid_constant__ CUtensorMap tm_P,
                const float* __restrict__ Dsum, T* __restrict__ dK, T* __restrict__ dV, int M, int N,
-               KernelStatus* status, uint64_t timeout_ns) {
+               int H, KernelStatus* status, uint64_t timeout_ns) {
   using Cfg = DkvCfg<D>;
   constexpr int kEpi = Cfg::kDSWarps;
   extern __shared__ uint8_t smem_raw[];
@@ -612,12 +614,14 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kTile;
-  const int h = blockIdx.y;
   const int mt = (M + kTile - 1) / kTile;
+  const int ntk = (N + kTile - 1) / kTile;
+  const int tiles = ntk * H;  // work items (key tile, head), head-major
 
   if (threadIdx.x == 0) {
     mbar_init(&bar[kKbV], 1);
+    mbar_init(&bar[kKbVEmpty], 1);
+    mbar_init(&bar[kKbAccEmpty], kEpi);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bar[kKbPFull0 + s], 1);
       mbar_init(&bar[kKbPEmpty0 + s], 1 + kEpi);
@@ -645,39 +649,50 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   WaitCtx ctx{abort_flag, timeout_ns};
 
+  // Every role walks the same work items: t = blockIdx.x, + gridDim.x, ...
+  // Shared-memory rings, TMEM buffers and their barrier phases continue
+  // across items (global step counter g over (item, query tile)).
   if (warp == 0) {
-    // ---- TMA producer: V_j once, then the P stream (2 slots).
+    // ---- TMA producer: per item V_j (once the previous item's dP^T MMAs are
+    // done), then the P stream (2 slots).
     if (lane == 0) {
       tma_prefetch_desc(&tm_V);
       tma_prefetch_desc(&tm_P);
       const uint64_t pol_p = l2_policy_evict_first();
       const uint64_t pol_v = l2_policy_evict_normal();
-      mbar_arrive_expect_tx(&bar[kKbV], Cfg::kMD);
-#pragma unroll
-      for (int b = 0; b < D / kBoxCols; ++b)
-        tma_load_3d(smem + Cfg::kOffV + b * kBoxBytes, &tm_V, &bar[kKbV], b * kBoxCols, n0, h, pol_v);
       constexpr int kAhead = 4;  // P tiles pulled into L2 ahead of the 2-slot ring
-      for (int i = 0; i < kAhead && i < mt; ++i) {
-        tma_prefetch_l2_3d(&tm_P, n0, i * kTile, h);
-        tma_prefetch_l2_3d(&tm_P, n0 + kBoxCols, i * kTile, h);
-      }
-      int issued = 0;
-      for (int i = 0; i < mt; ++i) {
-        const int s = i & 1;
-        const int u = i >> 1;
-        if (i + kAhead < mt) {
-          tma_prefetch_l2_3d(&tm_P, n0, (i + kAhead) * kTile, h);
-          tma_prefetch_l2_3d(&tm_P, n0 + kBoxCols, (i + kAhead) * kTile, h);
+      int g = 0, issued = 0, nv = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int h = t / ntk;
+        const int n0 = (t - h * ntk) * kTile;
+        for (int i = 0; i < kAhead && i < mt; ++i) {
+          tma_prefetch_l2_3d(&tm_P, n0, i * kTile, h);
+          tma_prefetch_l2_3d(&tm_P, n0 + kBoxCols, i * kTile, h);
         }
-        if (u > 0 && !mbar_wait(&bar[kKbPEmpty0 + s], (u - 1) & 1, ctx, 30)) break;
-        uint8_t* dst = smem + Cfg::kOffP + s * Cfg::kPT;
-        mbar_arrive_expect_tx(&bar[kKbPFull0 + s], Cfg::kPT);
-        tma_load_3d(dst, &tm_P, &bar[kKbPFull0 + s], n0, i * kTile, h, pol_p);
-        tma_load_3d(dst + kBoxBytes, &tm_P, &bar[kKbPFull0 + s], n0 + kBoxCols, i * kTile, h, pol_p);
-        ++issued;
+        if (nv > 0 && !mbar_wait(&bar[kKbVEmpty], (nv - 1) & 1, ctx, 32)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bar[kKbV], Cfg::kMD);
+#pragma unroll
+        for (int b = 0; b < D / kBoxCols; ++b)
+          tma_load_3d(smem + Cfg::kOffV + b * kBoxBytes, &tm_V, &bar[kKbV], b * kBoxCols, n0, h, pol_v);
+        ++nv;
+        for (int i = 0; i < mt; ++i, ++g) {
+          const int s = g & 1;
+          const int u = g >> 1;
+          if (i + kAhead < mt) {
+            tma_prefetch_l2_3d(&tm_P, n0, (i + kAhead) * kTile, h);
+            tma_prefetch_l2_3d(&tm_P, n0 + kBoxCols, (i + kAhead) * kTile, h);
+          }
+          if (u > 0 && !mbar_wait(&bar[kKbPEmpty0 + s], (u - 1) & 1, ctx, 30)) { ok = false; break; }
+          uint8_t* dst = smem + Cfg::kOffP + s * Cfg::kPT;
+          mbar_arrive_expect_tx(&bar[kKbPFull0 + s], Cfg::kPT);
+          tma_load_3d(dst, &tm_P, &bar[kKbPFull0 + s], n0, i * kTile, h, pol_p);
+          tma_load_3d(dst + kBoxBytes, &tm_P, &bar[kKbPFull0 + s], n0 + kBoxCols, i * kTile, h, pol_p);
+          ++issued;
+        }
       }
       if (*abort_flag) {
-        mbar_wait_drain(&bar[kKbV], 0, timeout_ns);
+        if (nv > 0) mbar_wait_drain(&bar[kKbV], (nv - 1) & 1, timeout_ns);
         for (int i = (issued > 2 ? issued - 2 : 0); i < issued; ++i)
           mbar_wait_drain(&bar[kKbPFull0 + (i & 1)], (i >> 1) & 1, timeout_ns);
       }
@@ -692,39 +707,52 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       tma_prefetch_desc(&tm_dO);
       tma_prefetch_desc(&tm_Q);
       const uint64_t pol = l2_policy_evict_last();
-      for (int i = 0; i < kL2Ahead && i < mt; ++i)
-        for (int b = 0; b < D / kBoxCols; ++b) {
-          tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, i * kTile, h);
-          tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, i * kTile, h);
-        }
+      {
+        const int h0 = static_cast<int>(blockIdx.x) / ntk;
+        for (int i = 0; i < kL2Ahead && i < mt; ++i)
+          for (int b = 0; b < D / kBoxCols; ++b) {
+            tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, i * kTile, h0);
+            tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, i * kTile, h0);
+          }
+      }
+      // global counters over (item, query tile); the query tile of step g is
+      // g % mt and its head is that of item blockIdx.x + (g / mt) * gridDim.x
+      const int my_items = (tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                           static_cast<int>(gridDim.x);
+      const int total = my_items * mt;
+      auto head_of = [&](int g) { return (static_cast<int>(blockIdx.x) + (g / mt) * static_cast<int>(gridDim.x)) / ntk; };
       int next_do = 0, next_q = 0;
       uint64_t t_last = global_timer_ns();
       bool failed = false;
-      while ((next_do < mt || next_q < mt) && !failed) {
+      while ((next_do < total || next_q < total) && !failed) {
         bool progressed = false;
-        if (next_do < mt && (next_do < 2 || mbar_poll(&bar[kKbDOEmpty0 + (next_do & 1)], ((next_do >> 1) - 1) & 1))) {
+        if (next_do < total && (next_do < 2 || mbar_poll(&bar[kKbDOEmpty0 + (next_do & 1)], ((next_do >> 1) - 1) & 1))) {
           const int s = next_do & 1;
+          const int hh = head_of(next_do), i = next_do % mt;
           mbar_arrive_expect_tx(&bar[kKbDOFull0 + s], Cfg::kMD);
 #pragma unroll
           for (int b = 0; b < D / kBoxCols; ++b)
             tma_load_3d(smem + Cfg::kOffdO + s * Cfg::kMD + b * kBoxBytes, &tm_dO, &bar[kKbDOFull0 + s],
-                        b * kBoxCols, next_do * kTile, h, pol);
-          if (next_do + kL2Ahead < mt)
+                        b * kBoxCols, i * kTile, hh, pol);
+          const int ahead = next_do + kL2Ahead;
+          if (ahead < total)
             for (int b = 0; b < D / kBoxCols; ++b)
-              tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, (next_do + kL2Ahead) * kTile, h);
+              tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, (ahead % mt) * kTile, head_of(ahead));
           ++next_do;
           progressed = true;
         }
-        if (next_q < mt && (next_q < 2 || mbar_poll(&bar[kKbQEmpty0 + (next_q & 1)], ((next_q >> 1) - 1) & 1))) {
+        if (next_q < total && (next_q < 2 || mbar_poll(&bar[kKbQEmpty0 + (next_q & 1)], ((next_q >> 1) - 1) & 1))) {
           const int s = next_q & 1;
+          const int hh = head_of(next_q), i = next_q % mt;
           mbar_arrive_expect_tx(&bar[kKbQFull0 + s], Cfg::kMD);
 #pragma unroll
           for (int b = 0; b < D / kBoxCols; ++b)
             tma_load_3d(smem + Cfg::kOffQ + s * Cfg::kMD + b * kBoxBytes, &tm_Q, &bar[kKbQFull0 + s],
-                        b * kBoxCols, next_q * kTile, h, pol);
-          if (next_q + kL2Ahead < mt)
+                        b * kBoxCols, i * kTile, hh, pol);
+          const int ahead = next_q + kL2Ahead;
+          if (ahead < total)
             for (int b = 0; b < D / kBoxCols; ++b)
-              tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, (next_q + kL2Ahead) * kTile, h);
+              tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, (ahead % mt) * kTile, head_of(ahead));
           ++next_q;
           progressed = true;
         }
@@ -758,13 +786,15 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       const uint32_t sV = smem_u32(smem + Cfg::kOffV);
       bool ok = true;
       if (warp == 1) {
-        ok = mbar_wait(&bar[kKbV], 0, ctx, 45);
-        for (int i = 0; i < mt && ok; ++i) {
-          const int s = i & 1;
+        int g = 0, tc = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+        if (!mbar_wait(&bar[kKbV], tc & 1, ctx, 45)) { ok = false; break; }
+        for (int i = 0; i < mt; ++i, ++g) {
+          const int s = g & 1;
           const uint32_t sdO = smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD);
-          if (!mbar_wait(&bar[kKbDOFull0 + s], (i >> 1) & 1, ctx, 40)) { ok = false; break; }
-          // buffer i % 2 is free once dK_{i-2} has read dS^T_{i-2} from it
-          if (i >= 2 && !mbar_wait(&bar[kKbXFree0 + s], ((i >> 1) - 1) & 1, ctx, 41)) { ok = false; break; }
+          if (!mbar_wait(&bar[kKbDOFull0 + s], (g >> 1) & 1, ctx, 40)) { ok = false; break; }
+          // buffer g % 2 is free once dK has read dS^T of step g - 2 from it
+          if (g >= 2 && !mbar_wait(&bar[kKbXFree0 + s], ((g >> 1) - 1) & 1, ctx, 41)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
@@ -775,18 +805,20 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           umma_commit(&bar[kKbXFull0 + s]);
           umma_commit(&bar[kKbDOEmpty0 + s]);
         }
+        if (ok) umma_commit(&bar[kKbVEmpty]);  // V_j consumed
+        }
         if (!ok) {
           umma_commit(&bar[kKbDrain]);
           mbar_wait_drain(&bar[kKbDrain], 0, timeout_ns);
         }
       } else {
-        auto issue_dV = [&](int i) -> bool {
-          const int s = i & 1;
+        auto issue_dV = [&](int i, int g) -> bool {
+          const int s = g & 1;
           const uint32_t sdO = smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD);
           const uint32_t sP = smem_u32(smem + Cfg::kOffP + s * Cfg::kPT);
           // dV += P_ij^T dO_i : A = P^T (MN-major, M = key), B = dO_i (MN-major, N = d).
-          if (!mbar_wait(&bar[kKbPFull0 + s], (i >> 1) & 1, ctx, 42)) return false;
-          if (!mbar_wait(&bar[kKbDOFull0 + s], (i >> 1) & 1, ctx, 46)) return false;
+          if (!mbar_wait(&bar[kKbPFull0 + s], (g >> 1) & 1, ctx, 42)) return false;
+          if (!mbar_wait(&bar[kKbDOFull0 + s], (g >> 1) & 1, ctx, 46)) return false;
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < kTile / 16; ++k) {
@@ -797,13 +829,13 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           umma_commit(&bar[kKbPEmpty0 + s]);
           return true;
         };
-        auto issue_dK = [&](int i) -> bool {
-          const int s = i & 1;
+        auto issue_dK = [&](int i, int g) -> bool {
+          const int s = g & 1;
           const uint32_t sQ = smem_u32(smem + Cfg::kOffQ + s * Cfg::kMD);
           // dK += dS^T Q_i : A = dS^T from TMEM buffer s (16 queries = 8
           // packed columns per step), B = Q_i (MN-major, N = d).
-          if (!mbar_wait(&bar[kKbQFull0 + s], (i >> 1) & 1, ctx, 43)) return false;
-          if (!mbar_wait(&bar[kKbEFull0 + s], (i >> 1) & 1, ctx, 44)) return false;
+          if (!mbar_wait(&bar[kKbQFull0 + s], (g >> 1) & 1, ctx, 43)) return false;
+          if (!mbar_wait(&bar[kKbEFull0 + s], (g >> 1) & 1, ctx, 44)) return false;
           tc_fence_after();
           const uint32_t tS = tmem + Cfg::kColX + 128 * s;
 #pragma unroll
@@ -815,14 +847,18 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           umma_commit(&bar[kKbXFree0 + s]);
           return true;
         };
-        ok = issue_dV(0);
-        for (int i = 0; i < mt && ok; ++i) {
-          if (!issue_dK(i)) { ok = false; break; }
-          if (i + 1 < mt && !issue_dV(i + 1)) { ok = false; break; }
+        int g = 0, tc = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc, g += mt) {
+          // dV and dK of the previous item must have been read out first
+          if (tc > 0 && !mbar_wait(&bar[kKbAccEmpty], (tc - 1) & 1, ctx, 47)) { ok = false; break; }
+          ok = issue_dV(0, g);
+          for (int i = 0; i < mt && ok; ++i) {
+            if (!issue_dK(i, g + i)) { ok = false; break; }
+            if (i + 1 < mt && !issue_dV(i + 1, g + i + 1)) { ok = false; break; }
+          }
+          if (ok) umma_commit(&bar[kKbAcc]);
         }
-        if (ok) {
-          umma_commit(&bar[kKbAcc]);
-        } else {
+        if (!ok) {
           umma_commit(&bar[kKbDrain2]);
           mbar_wait_drain(&bar[kKbDrain2], 0, timeout_ns);
         }
@@ -838,8 +874,12 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     const int c = (warp - Cfg::kFirstDSWarp) >> 2;
     const uint32_t lq = static_cast<uint32_t>(lane & 3);
     bool ok = true;
-    for (int i = 0; i < mt && ok; ++i) {
-      const int s = i & 1;
+    int g = 0, tc = 0;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+    const int h = t / ntk;
+    const int n0 = (t - h * ntk) * kTile;
+    for (int i = 0; i < mt; ++i, ++g) {
+      const int s = g & 1;
       // D for this thread's 16 queries (rows of the query tile past M read 0)
       float Dv[16];
       {
@@ -852,8 +892,8 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           Dv[2 * blk + 1] = q + 1 < M ? __ldg(Dsum + drow + q + 1) : 0.f;
         }
       }
-      if (!mbar_wait(&bar[kKbXFull0 + s], (i >> 1) & 1, ctx, 50)) { ok = false; break; }
-      if (!mbar_wait(&bar[kKbPFull0 + s], (i >> 1) & 1, ctx, 51)) { ok = false; break; }
+      if (!mbar_wait(&bar[kKbXFull0 + s], (g >> 1) & 1, ctx, 50)) { ok = false; break; }
+      if (!mbar_wait(&bar[kKbPFull0 + s], (g >> 1) & 1, ctx, 51)) { ok = false; break; }
       __syncwarp();
       tc_fence_after();
       const uint32_t sP = smem_u32(smem + Cfg::kOffP + s * Cfg::kPT);
@@ -902,8 +942,11 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         mbar_arrive(&bar[kKbPEmpty0 + s]);
       }
     }
-    // final dV_j and dK_j rows (lane = key row) -> 16-bit outputs
-    if (ok && mbar_wait(&bar[kKbAcc], 0, ctx, 53)) {
+    if (!ok) break;
+    // final dV_j and dK_j rows (lane = key row) -> 16-bit outputs, then hand
+    // the accumulators back to the issuer
+    if (!mbar_wait(&bar[kKbAcc], tc & 1, ctx, 53)) { ok = false; break; }
+    {
       __syncwarp();
       tc_fence_after();
       const int r = qq * 32 + lane;
@@ -922,6 +965,9 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         }
       }
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kKbAccEmpty]);
+    }
     }
   }
 

@@ -264,20 +264,21 @@ int enqueue_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, co
   // the dQ kernel is persistent: one CTA per SM walks the (query tile, head) items
   const long long items = static_cast<long long>(mt) * H;
   const dim3 grid_rows(static_cast<unsigned>(items < sms ? items : sms));
-  const dim3 grid_cols((N + kTile - 1) / kTile, H);
+  const long long kitems = static_cast<long long>((N + kTile - 1) / kTile) * H;
+  const dim3 grid_cols(static_cast<unsigned>(kitems < sms ? kitems : sms));
   mark(0);
   if (D == 128) {
     dq_kernel<T, 128><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
         mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
     mark(1);
     dkv_kernel<T, 128><<<grid_cols, DkvCfg<128>::kThreads, DkvCfg<128>::kSmemBytes, stream>>>(
-        mQ, mV, mdO, mP, dsum, dK, dV, M, N, st, tmo);
+        mQ, mV, mdO, mP, dsum, dK, dV, M, N, H, st, tmo);
   } else {
     dq_kernel<T, 64><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
         mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
     mark(1);
     dkv_kernel<T, 64><<<grid_cols, DkvCfg<64>::kThreads, DkvCfg<64>::kSmemBytes, stream>>>(
-        mQ, mV, mdO, mP, dsum, dK, dV, M, N, st, tmo);
+        mQ, mV, mdO, mP, dsum, dK, dV, M, N, H, st, tmo);
   }
   mark(2);
   mark(3);
