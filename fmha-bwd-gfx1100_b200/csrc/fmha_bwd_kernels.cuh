@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       constexpr uint32_t id_dP = make_idesc_f16<kB>(kTile, kTile, false, false);
       // A += E K_j, B += P K_j: K = keys, N = d; B operand K_j [key][d] is MN-major
       constexpr uint32_t id_AB = make_idesc_f16<kB>(kTile, D, false, true);
-      const uint32_t sdO = smem_u32(smem + Cfg::kOffdO);
+      const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO), 16, 1024);
       const uint32_t sV0 = smem_u32(smem + Cfg::kOffV);
       const uint32_t sK0 = smem_u32(smem + Cfg::kOffK);
       const uint32_t sP0 = smem_u32(smem + Cfg::kOffP);
@@ -346,13 +346,12 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
             if (!mbar_wait(&bar[kQbVFull0 + g % SV], (g / SV) & 1, ctx, 10)) { ok = false; break; }
             if (g >= 2 && !mbar_wait(&bar[kQbXFree0 + (g & 1)], ((g >> 1) - 1) & 1, ctx, 11)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sV = sV0 + (g % SV) * Cfg::kMD;
+            const uint64_t dV = make_sw128_desc(sV0 + (g % SV) * Cfg::kMD, 16, 1024);
             const uint32_t tX = tmem + Cfg::kColX + 128 * (g & 1);
 #pragma unroll
             for (int k = 0; k < D / 16; ++k) {
               const uint32_t off = (k >> 2) * kBoxBytes + (k & 3) * 32;
-              umma_f16_ss(tX, make_sw128_desc(sdO + off, 16, 1024), make_sw128_desc(sV + off, 16, 1024), id_dP,
-                          k > 0 ? 1u : 0u);
+              umma_f16_ss(tX, desc_advance(ddO, off), desc_advance(dV, off), id_dP, k > 0 ? 1u : 0u);
             }
             umma_commit(&bar[kQbXFull0 + (g & 1)]);
             umma_commit(&bar[kQbVEmpty0 + g % SV]);  // V_j consumed
@@ -370,12 +369,12 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
             if (!mbar_wait(&bar[kQbPFull0 + g % SP], (g / SP) & 1, ctx, 14)) { ok = false; break; }
             if (!mbar_wait(&bar[kQbKFull0 + g % SK], (g / SK) & 1, ctx, 15)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sP = sP0 + (g % SP) * Cfg::kPT;
-            const uint32_t sK = sK0 + (g % SK) * Cfg::kMD;
+            const uint64_t dP = make_sw128_desc(sP0 + (g % SP) * Cfg::kPT, 16, 1024);
+            const uint64_t dK = make_sw128_desc(sK0 + (g % SK) * Cfg::kMD, kBoxBytes, 1024);
 #pragma unroll
             for (int k = 0; k < kTile / 16; ++k) {
-              umma_f16_ss(tmem + Cfg::kColB, make_sw128_desc(sP + (k >> 2) * kBoxBytes + (k & 3) * 32, 16, 1024),
-                          make_sw128_desc(sK + k * 2048, kBoxBytes, 1024), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+              umma_f16_ss(tmem + Cfg::kColB, desc_advance(dP, (k >> 2) * kBoxBytes + (k & 3) * 32),
+                          desc_advance(dK, k * 2048), id_AB, (j > 0 || k > 0) ? 1u : 0u);
             }
             umma_commit(&bar[kQbPEmpty0 + g % SP]);  // the tensor core's read of P_ij
             if (!mbar_wait(&bar[kQbEFull0 + (g & 1)], (g >> 1) & 1, ctx, 12)) { ok = false; break; }
@@ -384,8 +383,8 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 #pragma unroll
             for (int k = 0; k < kTile / 16; ++k) {
               // E for keys 16k..16k+15 sits in key half (k >> 2): 8 columns per step
-              umma_f16_ts(tmem + Cfg::kColA, tE + (k >> 2) * 64 + (k & 3) * 8,
-                          make_sw128_desc(sK + k * 2048, kBoxBytes, 1024), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+              umma_f16_ts(tmem + Cfg::kColA, tE + (k >> 2) * 64 + (k & 3) * 8, desc_advance(dK, k * 2048), id_AB,
+                          (j > 0 || k > 0) ? 1u : 0u);
             }
             umma_commit(&bar[kQbKEmpty0 + g % SK]);  // K_j consumed (B_j and A_j)
             umma_commit(&bar[kQbXFree0 + (g & 1)]);
@@ -783,7 +782,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       constexpr uint32_t id_dP = make_idesc_f16<kB>(kTile, kTile, false, false);
       constexpr uint32_t id_dV = make_idesc_f16<kB>(kTile, D, true, true);
       constexpr uint32_t id_dK = make_idesc_f16<kB>(kTile, D, false, true);
-      const uint32_t sV = smem_u32(smem + Cfg::kOffV);
+      const uint64_t dVt = make_sw128_desc(smem_u32(smem + Cfg::kOffV), 16, 1024);
       bool ok = true;
       if (warp == 1) {
         int g = 0, tc = 0;
@@ -791,7 +790,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         if (!mbar_wait(&bar[kKbV], tc & 1, ctx, 45)) { ok = false; break; }
         for (int i = 0; i < mt; ++i, ++g) {
           const int s = g & 1;
-          const uint32_t sdO = smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD);
+          const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD), 16, 1024);
           if (!mbar_wait(&bar[kKbDOFull0 + s], (g >> 1) & 1, ctx, 40)) { ok = false; break; }
           // buffer g % 2 is free once dK has read dS^T of step g - 2 from it
           if (g >= 2 && !mbar_wait(&bar[kKbXFree0 + s], ((g >> 1) - 1) & 1, ctx, 41)) { ok = false; break; }
@@ -799,8 +798,8 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
             const uint32_t off = (k >> 2) * kBoxBytes + (k & 3) * 32;
-            umma_f16_ss(tmem + Cfg::kColX + 128 * s, make_sw128_desc(sV + off, 16, 1024),
-                        make_sw128_desc(sdO + off, 16, 1024), id_dP, k > 0 ? 1u : 0u);
+            umma_f16_ss(tmem + Cfg::kColX + 128 * s, desc_advance(dVt, off), desc_advance(ddO, off), id_dP,
+                        k > 0 ? 1u : 0u);
           }
           umma_commit(&bar[kKbXFull0 + s]);
           umma_commit(&bar[kKbDOEmpty0 + s]);
@@ -814,16 +813,16 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       } else {
         auto issue_dV = [&](int i, int g) -> bool {
           const int s = g & 1;
-          const uint32_t sdO = smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD);
-          const uint32_t sP = smem_u32(smem + Cfg::kOffP + s * Cfg::kPT);
+          const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD), kBoxBytes, 1024);
+          const uint64_t dP = make_sw128_desc(smem_u32(smem + Cfg::kOffP + s * Cfg::kPT), kBoxBytes, 1024);
           // dV += P_ij^T dO_i : A = P^T (MN-major, M = key), B = dO_i (MN-major, N = d).
           if (!mbar_wait(&bar[kKbPFull0 + s], (g >> 1) & 1, ctx, 42)) return false;
           if (!mbar_wait(&bar[kKbDOFull0 + s], (g >> 1) & 1, ctx, 46)) return false;
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < kTile / 16; ++k) {
-            umma_f16_ss(tmem + Cfg::kColdV, make_sw128_desc(sP + k * 2048, kBoxBytes, 1024),
-                        make_sw128_desc(sdO + k * 2048, kBoxBytes, 1024), id_dV, (i > 0 || k > 0) ? 1u : 0u);
+            umma_f16_ss(tmem + Cfg::kColdV, desc_advance(dP, k * 2048), desc_advance(ddO, k * 2048), id_dV,
+                        (i > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&bar[kKbDOEmpty0 + s]);
           umma_commit(&bar[kKbPEmpty0 + s]);
@@ -831,7 +830,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         };
         auto issue_dK = [&](int i, int g) -> bool {
           const int s = g & 1;
-          const uint32_t sQ = smem_u32(smem + Cfg::kOffQ + s * Cfg::kMD);
+          const uint64_t dQd = make_sw128_desc(smem_u32(smem + Cfg::kOffQ + s * Cfg::kMD), kBoxBytes, 1024);
           // dK += dS^T Q_i : A = dS^T from TMEM buffer s (16 queries = 8
           // packed columns per step), B = Q_i (MN-major, N = d).
           if (!mbar_wait(&bar[kKbQFull0 + s], (g >> 1) & 1, ctx, 43)) return false;
@@ -841,7 +840,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
 #pragma unroll
           for (int k = 0; k < kTile / 16; ++k) {
             umma_f16_ts(tmem + Cfg::kColdK, tS + (k >> 2) * 64 + (k & 3) * 8,
-                        make_sw128_desc(sQ + k * 2048, kBoxBytes, 1024), id_dK, (i > 0 || k > 0) ? 1u : 0u);
+                        desc_advance(dQd, k * 2048), id_dK, (i > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&bar[kKbQEmpty0 + s]);
           umma_commit(&bar[kKbXFree0 + s]);

@@ -488,6 +488,14 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr,
   return d;
 }
 
+// The same operand layout starting `bytes` further on. The start-address
+// field holds bits [4,18) of the shared-memory address, and addresses stay
+// below 256 KB, so adding bytes >> 4 never carries out of the field; with a
+// compile-time `bytes` this is a single add on the MMA-issuing path.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t bytes) {
+  return desc + static_cast<uint64_t>(bytes >> 4);
+}
+
 // Instruction descriptor for kind::f16 with fp32 accumulation.
 //   [4,6) D format (1 = F32); [7,10) A format; [10,13) B format
 //   (0 = F16, 1 = BF16); [15] A MN-major; [16] B MN-major;
