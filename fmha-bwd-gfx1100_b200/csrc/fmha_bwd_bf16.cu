@@ -69,6 +69,13 @@ FMHA_API int fmha_bwd_full_stream(bf16* dQ, bf16* dK, bf16* dV, const bf16* Q, c
                                         stream, /*sync=*/false);
 }
 
+FMHA_API int fmha_bwd_full_delta(bf16* dQ, bf16* dK, bf16* dV, const bf16* Q, const bf16* K,
+                                 const bf16* V, const bf16* P, const bf16* dO, const float* Dsum,
+                                 int M, int N, int K_dim, int total_heads, cudaStream_t stream) {
+  return fmha_sm100::run_backward<bf16>(dQ, dK, dV, Q, K, V, P, dO, M, N, K_dim, total_heads,
+                                        stream, /*sync=*/false, nullptr, Dsum, /*need_given_d=*/true);
+}
+
 FMHA_API int fmha_bwd_full_stream_events(bf16* dQ, bf16* dK, bf16* dV, const bf16* Q, const bf16* K,
                              const bf16* V, const bf16* P, const bf16* dO, int M, int N, int K_dim,
                              int total_heads, cudaStream_t stream, cudaEvent_t const* events) {

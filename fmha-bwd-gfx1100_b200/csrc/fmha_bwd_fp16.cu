@@ -22,6 +22,13 @@ FMHA_API int fmha_bwd_full_fp16_stream(fp16* dQ, fp16* dK, fp16* dV, const fp16*
                                         stream, /*sync=*/false);
 }
 
+FMHA_API int fmha_bwd_full_fp16_delta(fp16* dQ, fp16* dK, fp16* dV, const fp16* Q, const fp16* K,
+                                      const fp16* V, const fp16* P, const fp16* dO, const float* Dsum,
+                                      int M, int N, int K_dim, int total_heads, cudaStream_t stream) {
+  return fmha_sm100::run_backward<fp16>(dQ, dK, dV, Q, K, V, P, dO, M, N, K_dim, total_heads,
+                                        stream, /*sync=*/false, nullptr, Dsum, /*need_given_d=*/true);
+}
+
 FMHA_API int fmha_bwd_full_fp16_stream_events(fp16* dQ, fp16* dK, fp16* dV, const fp16* Q, const fp16* K,
                              const fp16* V, const fp16* P, const fp16* dO, int M, int N, int K_dim,
                              int total_heads, cudaStream_t stream, cudaEvent_t const* events) {

@@ -186,7 +186,11 @@ enum DqBar : int {
 };
 static_assert(kNumDqBars * 8 + 8 <= 512, "dq barrier area");
 
-template <typename T, int D>
+// kGivenD: D (rowsum of P * dP, one float per query row and head) is an
+// input; then E = P (dP - D) = dS, A = dS K = dQ directly, and neither the
+// B accumulation nor the rowsum is needed (5 instead of 6 GEMM-sized MMA
+// passes per call). Otherwise Dsum is written.
+template <typename T, int D, bool kGivenD = false>
 __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
     dq_kernel(const __grid_constant__ CUtensorMap tm_P, const __grid_constant__ CUtensorMap tm_V,
               const __grid_constant__ CUtensorMap tm_K, const __grid_constant__ CUtensorMap tm_dO,
@@ -366,17 +370,19 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
           if (tc > 0 && !mbar_wait(&bar[kQbAccEmpty], (tc - 1) & 1, ctx, 16)) { ok = false; break; }
           for (int j = 0; j < nt; ++j, ++g) {
-            if (!mbar_wait(&bar[kQbPFull0 + g % SP], (g / SP) & 1, ctx, 14)) { ok = false; break; }
+            if (!kGivenD && !mbar_wait(&bar[kQbPFull0 + g % SP], (g / SP) & 1, ctx, 14)) { ok = false; break; }
             if (!mbar_wait(&bar[kQbKFull0 + g % SK], (g / SK) & 1, ctx, 15)) { ok = false; break; }
             tc_fence_after();
-            const uint64_t dP = make_sw128_desc(sP0 + (g % SP) * Cfg::kPT, 16, 1024);
             const uint64_t dK = make_sw128_desc(sK0 + (g % SK) * Cfg::kMD, kBoxBytes, 1024);
+            if constexpr (!kGivenD) {
+              const uint64_t dP = make_sw128_desc(sP0 + (g % SP) * Cfg::kPT, 16, 1024);
 #pragma unroll
-            for (int k = 0; k < kTile / 16; ++k) {
-              umma_f16_ss(tmem + Cfg::kColB, desc_advance(dP, (k >> 2) * kBoxBytes + (k & 3) * 32),
-                          desc_advance(dK, k * 2048), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+              for (int k = 0; k < kTile / 16; ++k) {
+                umma_f16_ss(tmem + Cfg::kColB, desc_advance(dP, (k >> 2) * kBoxBytes + (k & 3) * 32),
+                            desc_advance(dK, k * 2048), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+              }
+              umma_commit(&bar[kQbPEmpty0 + g % SP]);  // the tensor core's read of P_ij
             }
-            umma_commit(&bar[kQbPEmpty0 + g % SP]);  // the tensor core's read of P_ij
             if (!mbar_wait(&bar[kQbEFull0 + (g & 1)], (g >> 1) & 1, ctx, 12)) { ok = false; break; }
             tc_fence_after();
             const uint32_t tE = tmem + Cfg::kColX + 128 * (g & 1);
@@ -388,6 +394,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
             }
             umma_commit(&bar[kQbKEmpty0 + g % SK]);  // K_j consumed (B_j and A_j)
             umma_commit(&bar[kQbXFree0 + (g & 1)]);
+            if (kGivenD) umma_commit(&bar[kQbPEmpty0 + g % SP]);  // keeps the slot's arrival count
           }
           if (ok) umma_commit(&bar[kQbAB]);  // A and B of this item complete
         }
@@ -431,7 +438,8 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       const int h = t / mt;
       const int m = (t - h * mt) * kTile + r;
       float Dacc = 0.f;   // this half's sum_n P dP over all key tiles
-      float shift = 0.f;  // c_i
+      float shift = 0.f;  // c_i (D_i itself when D is given)
+      if constexpr (kGivenD) shift = m < M ? Dsum[static_cast<int64_t>(h) * M + m] : 0.f;
       for (int j = 0; j < nt; ++j, ++g) {
         const int s = g % SP;
         const int b = g & 1;
@@ -448,19 +456,21 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
         for (int x = 0; x < 8; ++x) pv[x] = *reinterpret_cast<const uint4*>(pbox + sw128_offset(rsw, x));
         // sum_n P dP over this half tile
         float spdp = 0.f;
+        if constexpr (!kGivenD) {
 #pragma unroll
-        for (int x = 0; x < 8; ++x) {
-          const uint32_t pw[4] = {pv[x].x, pv[x].y, pv[x].z, pv[x].w};
-          const uint32_t* dp = x < 4 ? dpa + 8 * x : dpb + 8 * (x - 4);
+          for (int x = 0; x < 8; ++x) {
+            const uint32_t pw[4] = {pv[x].x, pv[x].y, pv[x].z, pv[x].w};
+            const uint32_t* dp = x < 4 ? dpa + 8 * x : dpb + 8 * (x - 4);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float2 p = Elem<T>::unpack(pw[u]);
-            spdp = fmaf(p.x, __uint_as_float(dp[2 * u]), spdp);
-            spdp = fmaf(p.y, __uint_as_float(dp[2 * u + 1]), spdp);
+            for (int u = 0; u < 4; ++u) {
+              const float2 p = Elem<T>::unpack(pw[u]);
+              spdp = fmaf(p.x, __uint_as_float(dp[2 * u]), spdp);
+              spdp = fmaf(p.y, __uint_as_float(dp[2 * u + 1]), spdp);
+            }
           }
+          Dacc += spdp;
         }
-        Dacc += spdp;
-        if (j == 0) {
+        if (!kGivenD && j == 0) {
           // shift c_i = P-weighted mean of dP over key tile 0 (both halves)
           float sp = 0.f;
 #pragma unroll
@@ -497,27 +507,37 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
         }
       }
       if (!ok) break;
-      // dQ = A - (D - c) B, and D; then hand A and B back to the issuer
+      // dQ = A - (D - c) B, and D (or dQ = A when D is given); then hand A
+      // and B back to the issuer
       if (!mbar_wait(&bar[kQbAB], tc & 1, ctx, 22)) { ok = false; break; }
       __syncwarp();
       tc_fence_after();
-      float Dother = 0.f;
-      if (!swap(Dacc, Dother)) { ok = false; break; }
-      const float Dfull = Dacc + Dother;
-      const float sD = Dfull - shift;
       constexpr int kHalf = D / 2;
       T* out = dQ + (static_cast<int64_t>(h) * M + m) * D + c * kHalf;
+      if constexpr (kGivenD) {
 #pragma unroll
-      for (int x = 0; x < kHalf / 32; ++x) {
-        uint32_t a[32], bb[32];
-        tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
-        tmem_load_32(lane_base + Cfg::kColB + c * kHalf + 32 * x, bb);
-        float v[32];
+        for (int x = 0; x < kHalf / 32; ++x) {
+          uint32_t a[32];
+          tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
+          if (m < M) store_row_32<T>(out + 32 * x, reinterpret_cast<const float*>(a));
+        }
+      } else {
+        float Dother = 0.f;
+        if (!swap(Dacc, Dother)) { ok = false; break; }
+        const float Dfull = Dacc + Dother;
+        const float sD = Dfull - shift;
 #pragma unroll
-        for (int y = 0; y < 32; ++y) v[y] = fmaf(-sD, __uint_as_float(bb[y]), __uint_as_float(a[y]));
-        if (m < M) store_row_32<T>(out + 32 * x, v);
+        for (int x = 0; x < kHalf / 32; ++x) {
+          uint32_t a[32], bb[32];
+          tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
+          tmem_load_32(lane_base + Cfg::kColB + c * kHalf + 32 * x, bb);
+          float v[32];
+#pragma unroll
+          for (int y = 0; y < 32; ++y) v[y] = fmaf(-sD, __uint_as_float(bb[y]), __uint_as_float(a[y]));
+          if (m < M) store_row_32<T>(out + 32 * x, v);
+        }
+        if (c == 0 && m < M) Dsum[static_cast<int64_t>(h) * M + m] = Dfull;
       }
-      if (c == 0 && m < M) Dsum[static_cast<int64_t>(h) * M + m] = Dfull;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kQbAccEmpty]);

@@ -151,6 +151,10 @@ inline uint64_t effective_timeout_ns() {
 
 template <typename T>
 void set_kernel_attrs() {
+  cudaFuncSetAttribute(dq_kernel<T, 64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       DqCfg<64>::kSmemBytes);
+  cudaFuncSetAttribute(dq_kernel<T, 128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       DqCfg<128>::kSmemBytes);
   cudaFuncSetAttribute(dq_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        DqCfg<64>::kSmemBytes);
   cudaFuncSetAttribute(dq_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -237,13 +241,15 @@ inline int check_args(const void* dQ, const void* dK, const void* dV, const void
 }
 
 // Encodes the tensor maps and enqueues the two kernels on `stream`, with D
-// at `dsum` and the wait status at `st`. Arguments are already checked.
+// at `dsum` (written by the dQ kernel, or read by both kernels when
+// `given_d` is set) and the wait status at `st`. Arguments are already
+// checked.
 // Optional timing events: [0] before the dQ kernel, [1] between the two
 // kernels, [2] and [3] after the dK/dV kernel.
 template <typename T>
 int enqueue_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const T* P,
                      const T* dO, int M, int N, int D, int H, float* dsum, KernelStatus* st,
-                     cudaStream_t stream, cudaEvent_t const* events) {
+                     cudaStream_t stream, cudaEvent_t const* events, bool given_d = false) {
   constexpr bool kBF16 = Elem<T>::kBF16;
   CUtensorMap mQ, mK, mV, mdO, mP;
   if (!encode_fn()) return set_error(kErrNoDriver, "cuTensorMapEncodeTiled is unavailable");
@@ -268,14 +274,22 @@ int enqueue_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, co
   const dim3 grid_cols(static_cast<unsigned>(kitems < sms ? kitems : sms));
   mark(0);
   if (D == 128) {
-    dq_kernel<T, 128><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
-        mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
+    if (given_d)
+      dq_kernel<T, 128, true><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
+          mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
+    else
+      dq_kernel<T, 128><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
+          mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
     mark(1);
     dkv_kernel<T, 128><<<grid_cols, DkvCfg<128>::kThreads, DkvCfg<128>::kSmemBytes, stream>>>(
         mQ, mV, mdO, mP, dsum, dK, dV, M, N, H, st, tmo);
   } else {
-    dq_kernel<T, 64><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
-        mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
+    if (given_d)
+      dq_kernel<T, 64, true><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
+          mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
+    else
+      dq_kernel<T, 64><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
+          mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
     mark(1);
     dkv_kernel<T, 64><<<grid_cols, DkvCfg<64>::kThreads, DkvCfg<64>::kSmemBytes, stream>>>(
         mQ, mV, mdO, mP, dsum, dK, dV, M, N, H, st, tmo);
@@ -310,12 +324,16 @@ __global__ void wait_selftest_kernel(KernelStatus* status, uint64_t timeout_ns) 
 
 // Launches the two kernels on `stream`. When `sync` is set, waits for the
 // stream and reports in-kernel wait timeouts as kErrDeviceTimeout.
+// `given_d`, when not null, is D = rowsum(P * dP) (fp32, [H][M]) supplied by
+// the caller; the dQ kernel then skips the rowsum and the B accumulation.
 template <typename T>
 int run_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const T* P,
                  const T* dO, int M, int N, int D, int H, cudaStream_t stream, bool sync,
-                 cudaEvent_t const* events = nullptr) {
+                 cudaEvent_t const* events = nullptr, const float* given_d = nullptr,
+                 bool need_given_d = false) {
   int rc = check_args(dQ, dK, dV, Q, K, V, P, dO, M, N, D, H);
   if (rc != kOk) return rc;
+  if (need_given_d && !given_d) return set_error(kErrInvalidArgument, "null D argument");
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) {
     cudaGetLastError();
@@ -328,12 +346,13 @@ int run_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const 
     return set_error(kErrUnsupportedDevice, "device %d is sm_%d%d; this library needs sm_100", device,
                      major, minor);
   const size_t rows = static_cast<size_t>(H) * static_cast<size_t>(M);
-  DeviceWorkspace* w = get_workspace<T>(device, rows);
+  DeviceWorkspace* w = get_workspace<T>(device, given_d ? 0 : rows);
   if (!w) return kErrOutOfMemory;
 
   if (sync) memset(w->host_status, 0, sizeof(KernelStatus));
-  rc = enqueue_backward<T>(dQ, dK, dV, Q, K, V, P, dO, M, N, D, H, w->dsum, w->host_status_dev,
-                           stream, events);
+  rc = enqueue_backward<T>(dQ, dK, dV, Q, K, V, P, dO, M, N, D, H,
+                           given_d ? const_cast<float*>(given_d) : w->dsum, w->host_status_dev,
+                           stream, events, given_d != nullptr);
   if (rc != kOk) return rc;
   cudaError_t e = cudaSuccess;
   if (sync) {

@@ -36,6 +36,11 @@ LIB_NAMES = {
     torch.bfloat16: ("libfmha_bwd_bf16.so", "fmha_bwd_full_py", "fmha_bwd_full_stream"),
     torch.float16: ("libfmha_bwd_fp16.so", "fmha_bwd_full_fp16", "fmha_bwd_full_fp16_stream"),
 }
+# precomputed-rowsum entries (additive to the reference's ABI)
+DELTA_NAMES = {
+    torch.bfloat16: "fmha_bwd_full_delta",
+    torch.float16: "fmha_bwd_full_fp16_delta",
+}
 
 ERROR_NAMES = {
     0: "OK",
@@ -83,6 +88,9 @@ def load_library(dtype: torch.dtype = torch.bfloat16) -> ctypes.CDLL:
     getattr(lib, full).restype = None
     getattr(lib, stream).argtypes = _PTR_ARGS + _INT_ARGS + [ctypes.c_void_p]
     getattr(lib, stream).restype = ctypes.c_int
+    delta = DELTA_NAMES[dtype]
+    getattr(lib, delta).argtypes = _PTR_ARGS + [ctypes.c_void_p] + _INT_ARGS + [ctypes.c_void_p]
+    getattr(lib, delta).restype = ctypes.c_int
     lib.fmha_bwd_last_error.argtypes = []
     lib.fmha_bwd_last_error.restype = ctypes.c_int
     lib.fmha_bwd_last_error_message.argtypes = []
@@ -93,6 +101,14 @@ def load_library(dtype: torch.dtype = torch.bfloat16) -> ctypes.CDLL:
     lib.fmha_bwd_set_wait_timeout_ms.restype = None
     _LIBS[path] = lib
     return lib
+
+
+def rowsum_delta(P, dO, V):
+    """D = rowsum(P * (dO V^T)) in fp32, [H, M] (reference formula,
+    cpu_reference.hpp:32-35), computed with torch for callers and tests of
+    the precomputed-rowsum entry."""
+    dP = torch.einsum("...mk,...nk->...mn", dO.float(), V.float())
+    return (dP * P.float()).sum(dim=-1).contiguous()
 
 
 def last_error(dtype: torch.dtype = torch.bfloat16) -> tuple[int, str]:
@@ -117,7 +133,7 @@ def _check_inputs(Q, K, V, P, dO):
             raise TypeError(f"{name} has dtype {t.dtype}, expected {Q.dtype}")
 
 
-def fmha_bwd(Q, K, V, P, dO, *, out=None, stream=None, sync: bool = True):
+def fmha_bwd(Q, K, V, P, dO, *, out=None, stream=None, sync: bool = True, delta=None):
     """Backward of attention for head-flattened tensors.
 
     Q, dO: [H, M, d]; K, V: [H, N, d]; P: [H, M, N] (any leading shape that
@@ -127,6 +143,10 @@ def fmha_bwd(Q, K, V, P, dO, *, out=None, stream=None, sync: bool = True):
     (``fmha_bwd_full_py`` / ``fmha_bwd_full_fp16``), which returns after the
     work has finished; with ``sync=False`` it uses the stream-ordered entry
     on ``stream`` (default: torch's current stream) and returns at once.
+    ``delta``, when given, is D = rowsum(P * dP) (equivalently rowsum(dO * O)
+    for the forward output O), an fp32 CUDA tensor of H*M elements; the
+    precomputed-rowsum entry then skips the rowsum and one GEMM-sized pass
+    (stream-ordered; synchronised afterwards when ``sync`` is set).
     """
     _check_inputs(Q, K, V, P, dO)
     d = Q.shape[-1]
@@ -144,6 +164,17 @@ def fmha_bwd(Q, K, V, P, dO, *, out=None, stream=None, sync: bool = True):
     args = (dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), Q.data_ptr(), K.data_ptr(),
             V.data_ptr(), P.data_ptr(), dO.data_ptr(), M, N, d, H)
     _, full, stream_fn = LIB_NAMES[Q.dtype]
+    if delta is not None:
+        if not delta.is_cuda or delta.dtype != torch.float32 or not delta.is_contiguous() \
+                or delta.numel() != H * M:
+            raise ValueError("delta must be a contiguous fp32 CUDA tensor of H*M elements")
+        s = stream if stream is not None else torch.cuda.current_stream(Q.device)
+        rc = getattr(lib, DELTA_NAMES[Q.dtype])(*args[:8], delta.data_ptr(), *args[8:],
+                                               ctypes.c_void_p(s.cuda_stream))
+        _raise_if_error(lib, rc)
+        if sync:
+            s.synchronize()
+        return dQ, dK, dV
     if sync:
         getattr(lib, full)(*args)
         _raise_if_error(lib)

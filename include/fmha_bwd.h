@@ -84,6 +84,19 @@ int fmha_bwd_full_stream_events(fmha_bf16_t* dQ, fmha_bf16_t* dK,
                                 int M, int N, int K_dim, int total_heads,
                                 fmha_stream_t stream, void* const* events);
 
+/* Precomputed-rowsum variant of fmha_bwd_full_stream (the "accept a
+ * precomputed D" extension the reference's path lacks; no reference
+ * counterpart). Dsum[h * M + m] = sum_n P[h,m,n] * dP[h,m,n] in fp32, i.e.
+ * rowsum(dO * O) when O = P V is the forward output, supplied by the caller
+ * (16-byte aligned device memory, read only). The dQ kernel then skips its
+ * own rowsum and the extra P K accumulation (5 instead of 6 GEMM-sized MMA
+ * passes). Stream-ordered; returns 0 or an error code (1 if Dsum is null). */
+int fmha_bwd_full_delta(fmha_bf16_t* dQ, fmha_bf16_t* dK, fmha_bf16_t* dV,
+                        const fmha_bf16_t* Q, const fmha_bf16_t* K,
+                        const fmha_bf16_t* V, const fmha_bf16_t* P,
+                        const fmha_bf16_t* dO, const float* Dsum, int M, int N,
+                        int K_dim, int total_heads, fmha_stream_t stream);
+
 /* No counterpart in the reference. Allocation-free variant of
  * fmha_bwd_full_stream: the fp32 rowsum scratch D (total_heads * M floats)
  * and the wait-status slot live in file-scope __device__ arrays of the
@@ -117,6 +130,14 @@ int fmha_bwd_full_fp16_stream(fmha_fp16_t* dQ, fmha_fp16_t* dK,
                               const fmha_fp16_t* P, const fmha_fp16_t* dO,
                               int M, int N, int K_dim, int total_heads,
                               fmha_stream_t stream);
+
+/* fp16 precomputed-rowsum variant, as fmha_bwd_full_delta. */
+int fmha_bwd_full_fp16_delta(fmha_fp16_t* dQ, fmha_fp16_t* dK, fmha_fp16_t* dV,
+                             const fmha_fp16_t* Q, const fmha_fp16_t* K,
+                             const fmha_fp16_t* V, const fmha_fp16_t* P,
+                             const fmha_fp16_t* dO, const float* Dsum, int M,
+                             int N, int K_dim, int total_heads,
+                             fmha_stream_t stream);
 
 /* fp16 profiling variant, as fmha_bwd_full_stream_events. */
 int fmha_bwd_full_fp16_stream_events(fmha_fp16_t* dQ, fmha_fp16_t* dK,

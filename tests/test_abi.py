@@ -132,3 +132,15 @@ def test_selftest_rejects_bad_timeout_without_gpu(kind):
     f.restype = ctypes.c_int
     assert f(0) == 1
     assert f(20000) == 1
+
+
+@pytest.mark.parametrize("kind,fn", [("bf16", "fmha_bwd_full_delta"), ("fp16", "fmha_bwd_full_fp16_delta")])
+def test_delta_entry_requires_rowsum(kind, fn):
+    """The precomputed-rowsum entry rejects a null D before touching the GPU."""
+    _ensure_built()
+    lib = ctypes.CDLL(LIBS[kind])
+    f = getattr(lib, fn)
+    f.argtypes = [ctypes.c_void_p] * 9 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    f.restype = ctypes.c_int
+    good = [0x10000 * (i + 1) for i in range(8)]
+    assert f(*good, None, 128, 128, 64, 2, None) == 1

@@ -134,6 +134,28 @@ def test_full_size_workloads(F, oracle_built, wname):
         _assert_ok(O, "dV", _f32(dV[sl]), ov, w.dtype)
 
 
+def test_long_sequence_64bit_offsets(F, oracle_built):
+    """The long video shape (M = N = 16384, d = 128) with 10 heads: the last
+    head's P starts 2.4e9 elements in, past 2^31, so every per-head offset
+    must be 64-bit (the reference's int products overflow here). First and
+    last heads against the fp32 GPU recompute."""
+    import workloads
+
+    O = oracle_built
+    w = workloads.Workload("video10", 16384, 16384, 128, 10, "bf16")
+    assert (w.heads - 1) * w.M * w.N > 2**31
+    Q, K, V, P, dO = workloads.make_inputs(w, seed=7)
+    dQ, dK, dV = F.fmha_bwd(Q, K, V, P, dO)
+    torch.cuda.synchronize()
+    for h in (0, w.heads - 1):
+        sl = slice(h, h + 1)
+        rq, rk, rv = _torch_reference(Q[sl], K[sl], V[sl], P[sl], dO[sl])
+        _assert_ok(O, "dQ", _f32(dQ[sl]), rq.cpu().numpy(), "bf16")
+        _assert_ok(O, "dK", _f32(dK[sl]), rk.cpu().numpy(), "bf16")
+        _assert_ok(O, "dV", _f32(dV[sl]), rv.cpu().numpy(), "bf16")
+        del rq, rk, rv
+
+
 def test_outputs_fully_overwritten_and_repeatable(F, oracle_built):
     """NaN-filled outputs are fully overwritten; dK/dV are bit-identical
     across calls (no atomics there) and dQ agrees to fp32 reduction order."""
@@ -225,3 +247,31 @@ def test_bounded_wait_gives_up_and_context_survives(F, oracle_built, dtype):
     ref = O.oracle_bwd(Qb, Kb, Vb, Pb, dOb, name)
     for nm, got, r in zip(("dQ", "dK", "dV"), (dQ, dK, dV), ref[:3]):
         _assert_ok(O, nm, _f32(got), r, name)
+
+
+@pytest.mark.parametrize("M,N,d,H,dtype", [(1000, 520, 128, 2, torch.bfloat16),
+                                          (640, 1024, 64, 3, torch.float16),
+                                          (4608, 4608, 128, 3, torch.bfloat16)])
+def test_precomputed_rowsum_entry(F, oracle_built, M, N, d, H, dtype):
+    """fmha_bwd_full_delta / _fp16_delta with D = rowsum(P * dP) from the
+    caller: same outputs as the standard entry within the dtype tolerance,
+    and against the oracle."""
+    O = oracle_built
+    name = "bf16" if dtype == torch.bfloat16 else "fp16"
+    bits = O.make_inputs(M, N, d, H, name, seed=41) if M * H <= 4096 else None
+    if bits is not None:
+        Q, K, V, P, dO = (_to_dev(x, dtype) for x in bits)
+    else:
+        import workloads
+
+        w = workloads.Workload("sq", M, N, d, H, name)
+        Q, K, V, P, dO = workloads.make_inputs(w, seed=41)
+    delta = F.rowsum_delta(P, dO, V)
+    a = F.fmha_bwd(Q, K, V, P, dO)
+    b = F.fmha_bwd(Q, K, V, P, dO, delta=delta)
+    for nm, x, y in zip(("dQ", "dK", "dV"), a, b):
+        _assert_ok(O, nm, _f32(y), _f32(x), name)
+    if bits is not None:
+        ref = O.oracle_bwd(*bits, name)
+        for nm, got, r in zip(("dQ", "dK", "dV"), b, ref[:3]):
+            _assert_ok(O, nm, _f32(got), r, name)
