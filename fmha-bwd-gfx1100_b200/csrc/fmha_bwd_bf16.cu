@@ -4,6 +4,7 @@
 
 #include "fmha_bwd_common_abi.cuh"
 #include "fmha_bwd_launch.cuh"
+#include "fmha_bwd_stages.cuh"
 
 using bf16 = __nv_bfloat16;
 
@@ -135,6 +136,35 @@ FMHA_API int fmha_bwd_full_noalloc(bf16* dQ, bf16* dK, bf16* dV, const bf16* Q, 
     return set_error(kErrDeviceTimeout, "in-kernel wait gave up (code %d, site %d, block %d)",
                      st.code, st.where, st.block);
   return set_error(kOk, "");
+}
+
+// ---- stage hooks (replace the reference's test_* wrappers, src/fmha_bwd_kernels.hip:525-560).
+// Each launches one stage on the legacy default stream and returns without
+// waiting, like the reference; errors go to fmha_bwd_last_error().
+
+FMHA_API void test_dp_kernel(const bf16* dO, const bf16* V, bf16* dP, int M, int N, int K_dim,
+                               int total_heads) {
+  fmha_sm100::run_stage_gemm<bf16>(fmha_sm100::Stage::kDp, dO, V, dP, M, N, K_dim, total_heads);
+}
+
+FMHA_API void test_softmax_bwd_kernel(const bf16* P, const bf16* dP, bf16* dS, int M, int N,
+                                        int total_heads) {
+  fmha_sm100::run_stage_softmax_bwd<bf16>(P, dP, dS, M, N, total_heads);
+}
+
+FMHA_API void test_dq_kernel(const bf16* dS, const bf16* K, bf16* dQ, int M, int N, int K_dim,
+                               int total_heads) {
+  fmha_sm100::run_stage_gemm<bf16>(fmha_sm100::Stage::kDq, dS, K, dQ, M, N, K_dim, total_heads);
+}
+
+FMHA_API void test_dk_kernel(const bf16* dS, const bf16* Q, bf16* dK, int M, int N, int K_dim,
+                               int total_heads) {
+  fmha_sm100::run_stage_gemm<bf16>(fmha_sm100::Stage::kDk, dS, Q, dK, M, N, K_dim, total_heads);
+}
+
+FMHA_API void test_dv_kernel(const bf16* P, const bf16* dO, bf16* dV, int M, int N, int K_dim,
+                               int total_heads) {
+  fmha_sm100::run_stage_gemm<bf16>(fmha_sm100::Stage::kDv, P, dO, dV, M, N, K_dim, total_heads);
 }
 
 }  // extern "C"

@@ -4,6 +4,7 @@
 
 #include "fmha_bwd_common_abi.cuh"
 #include "fmha_bwd_launch.cuh"
+#include "fmha_bwd_stages.cuh"
 
 using fp16 = __half;
 
@@ -34,6 +35,36 @@ FMHA_API int fmha_bwd_full_fp16_stream_events(fp16* dQ, fp16* dK, fp16* dV, cons
                              int total_heads, cudaStream_t stream, cudaEvent_t const* events) {
   return fmha_sm100::run_backward<fp16>(dQ, dK, dV, Q, K, V, P, dO, M, N, K_dim, total_heads,
                                         stream, /*sync=*/false, events);
+}
+
+// ---- stage hooks (replace the reference's test_* wrappers, src/fmha_bwd_kernels_fp16.hip:284-314; C++ linkage there,
+// C linkage here).
+// Each launches one stage on the legacy default stream and returns without
+// waiting, like the reference; errors go to fmha_bwd_last_error().
+
+FMHA_API void test_dp_kernel_fp16(const fp16* dO, const fp16* V, fp16* dP, int M, int N, int K_dim,
+                               int total_heads) {
+  fmha_sm100::run_stage_gemm<fp16>(fmha_sm100::Stage::kDp, dO, V, dP, M, N, K_dim, total_heads);
+}
+
+FMHA_API void test_softmax_bwd_kernel_fp16(const fp16* P, const fp16* dP, fp16* dS, int M, int N,
+                                        int total_heads) {
+  fmha_sm100::run_stage_softmax_bwd<fp16>(P, dP, dS, M, N, total_heads);
+}
+
+FMHA_API void test_dq_kernel_fp16(const fp16* dS, const fp16* K, fp16* dQ, int M, int N, int K_dim,
+                               int total_heads) {
+  fmha_sm100::run_stage_gemm<fp16>(fmha_sm100::Stage::kDq, dS, K, dQ, M, N, K_dim, total_heads);
+}
+
+FMHA_API void test_dk_kernel_fp16(const fp16* dS, const fp16* Q, fp16* dK, int M, int N, int K_dim,
+                               int total_heads) {
+  fmha_sm100::run_stage_gemm<fp16>(fmha_sm100::Stage::kDk, dS, Q, dK, M, N, K_dim, total_heads);
+}
+
+FMHA_API void test_dv_kernel_fp16(const fp16* P, const fp16* dO, fp16* dV, int M, int N, int K_dim,
+                               int total_heads) {
+  fmha_sm100::run_stage_gemm<fp16>(fmha_sm100::Stage::kDv, P, dO, dV, M, N, K_dim, total_heads);
 }
 
 }  // extern "C"

@@ -185,6 +185,68 @@ def fmha_bwd(Q, K, V, P, dO, *, out=None, stream=None, sync: bool = True, delta=
     return dQ, dK, dV
 
 
+# ---------------------------------------------------------------- stage hooks
+# The reference's test_* wrappers (src/fmha_bwd_kernels.hip:525-560,
+# src/fmha_bwd_kernels_fp16.hip:284-314), one stage per launch with its
+# 16-bit intermediate in global memory. bf16 names have no suffix, fp16
+# names end in _fp16.
+STAGE_NAMES = ("dp", "softmax_bwd", "dq", "dk", "dv")
+
+
+def _stage_fn(lib: ctypes.CDLL, dtype: torch.dtype, stage: str):
+    name = f"test_{stage}_kernel" + ("_fp16" if dtype == torch.float16 else "")
+    f = getattr(lib, name)
+    if stage == "softmax_bwd":
+        f.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3
+    else:
+        f.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 4
+    f.restype = None
+    return f
+
+
+def run_stage(stage: str, a, b, *, sync: bool = True):
+    """Run one stage hook on [H, rows, cols] inputs in the reference's
+    argument order and return its output:
+      dp (dO, V) -> dP [H,M,N];  softmax_bwd (P, dP) -> dS [H,M,N];
+      dq (dS, K) -> dQ [H,M,d];  dk (dS, Q) -> dK [H,N,d];
+      dv (P, dO) -> dV [H,N,d].
+    The hook launches on the legacy default stream; with ``sync`` the call
+    waits for it and raises on an error or an in-kernel wait timeout."""
+    if stage not in STAGE_NAMES:
+        raise ValueError(f"unknown stage {stage!r}; one of {STAGE_NAMES}")
+    for name, t in (("a", a), ("b", b)):
+        if not t.is_cuda or not t.is_contiguous() or t.dtype != a.dtype or t.dim() < 3:
+            raise ValueError(f"{name} must be a contiguous CUDA tensor [H, rows, cols] of {a.dtype}")
+    lib = load_library(a.dtype)
+    H = a.shape[:-2].numel()
+    if stage == "dp":  # dO [H,M,d], V [H,N,d]
+        M, d = a.shape[-2:]
+        N = b.shape[-2]
+        out = torch.empty(*a.shape[:-1], N, dtype=a.dtype, device=a.device)
+        ints = (M, N, d, H)
+    elif stage == "softmax_bwd":  # P, dP [H,M,N]
+        M, N = a.shape[-2:]
+        out = torch.empty_like(a)
+        ints = (M, N, H)
+    elif stage == "dq":  # dS [H,M,N], K [H,N,d]
+        M, N = a.shape[-2:]
+        d = b.shape[-1]
+        out = torch.empty(*a.shape[:-1], d, dtype=a.dtype, device=a.device)
+        ints = (M, N, d, H)
+    else:  # dk: dS [H,M,N], Q [H,M,d]; dv: P [H,M,N], dO [H,M,d]
+        M, N = a.shape[-2:]
+        d = b.shape[-1]
+        out = torch.empty(*a.shape[:-2], N, d, dtype=a.dtype, device=a.device)
+        ints = (M, N, d, H)
+    _stage_fn(lib, a.dtype, stage)(a.data_ptr(), b.data_ptr(), out.data_ptr(), *ints)
+    _raise_if_error(lib)
+    if sync:
+        torch.cuda.synchronize(a.device)
+        if lib.fmha_bwd_poll_device_status() != 0:
+            raise FmhaBwdError(6, f"stage {stage}: an in-kernel wait gave up")
+    return out
+
+
 def custom_flash_attn_backward(Q, K, V, P, dO):
     """Mirror of the reference's custom_flash_attn_backward
     (benchmark_pytorch_final.py:39-53) for [batch, heads, M, d] inputs.

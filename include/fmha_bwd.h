@@ -114,6 +114,36 @@ int fmha_bwd_full_noalloc(fmha_bf16_t* dQ, fmha_bf16_t* dK, fmha_bf16_t* dV,
                           const fmha_bf16_t* dO, int M, int N, int K_dim,
                           int total_heads, fmha_stream_t stream);
 
+/* Stage hooks (replace the reference's test_* wrappers,
+ * src/fmha_bwd_kernels.hip:525-560). Each runs one stage of the backward as
+ * its own launch with its 16-bit intermediate in global memory ([H][M][N]
+ * for dP and dS), on the legacy default stream, and returns without waiting,
+ * as the reference does. Same layout and preconditions as fmha_bwd_full_py
+ * (N % 8 == 0, K_dim 64 or 128, 16-byte aligned pointers); a rejected call
+ * launches nothing and sets fmha_bwd_last_error(); in-kernel wait timeouts
+ * are read with fmha_bwd_poll_device_status() after the stream finished.
+ * The production entry points never use them (dP and dS stay on chip). */
+
+/* dP = dO V^T (src/fmha_bwd_kernels.hip:525-529). */
+void test_dp_kernel(const fmha_bf16_t* dO, const fmha_bf16_t* V, fmha_bf16_t* dP,
+                    int M, int N, int K_dim, int total_heads);
+
+/* dS = P * (dP - rowsum(P * dP)), rowsum in fp32 (:531-536). */
+void test_softmax_bwd_kernel(const fmha_bf16_t* P, const fmha_bf16_t* dP,
+                             fmha_bf16_t* dS, int M, int N, int total_heads);
+
+/* dQ = dS K (:538-542). */
+void test_dq_kernel(const fmha_bf16_t* dS, const fmha_bf16_t* K, fmha_bf16_t* dQ,
+                    int M, int N, int K_dim, int total_heads);
+
+/* dK = dS^T Q (:544-548). */
+void test_dk_kernel(const fmha_bf16_t* dS, const fmha_bf16_t* Q, fmha_bf16_t* dK,
+                    int M, int N, int K_dim, int total_heads);
+
+/* dV = P^T dO (:550-554; the reference names the last size BK_dim). */
+void test_dv_kernel(const fmha_bf16_t* P, const fmha_bf16_t* dO, fmha_bf16_t* dV,
+                    int M, int N, int K_dim, int total_heads);
+
 /* ---- libfmha_bwd_fp16.so ------------------------------------------------ */
 
 /* Replaces fmha_bwd_full_fp16, src/fmha_bwd_kernels_fp16.hip:236-238. */
@@ -146,6 +176,19 @@ int fmha_bwd_full_fp16_stream_events(fmha_fp16_t* dQ, fmha_fp16_t* dK,
                                      const fmha_fp16_t* P, const fmha_fp16_t* dO,
                                      int M, int N, int K_dim, int total_heads,
                                      fmha_stream_t stream, void* const* events);
+
+/* fp16 stage hooks, as the bf16 ones (src/fmha_bwd_kernels_fp16.hip:284-314,
+ * where they have C++ linkage; here they are plain C symbols). */
+void test_dp_kernel_fp16(const fmha_fp16_t* dO, const fmha_fp16_t* V, fmha_fp16_t* dP,
+                         int M, int N, int K_dim, int total_heads);
+void test_softmax_bwd_kernel_fp16(const fmha_fp16_t* P, const fmha_fp16_t* dP,
+                                  fmha_fp16_t* dS, int M, int N, int total_heads);
+void test_dq_kernel_fp16(const fmha_fp16_t* dS, const fmha_fp16_t* K, fmha_fp16_t* dQ,
+                         int M, int N, int K_dim, int total_heads);
+void test_dk_kernel_fp16(const fmha_fp16_t* dS, const fmha_fp16_t* Q, fmha_fp16_t* dK,
+                         int M, int N, int K_dim, int total_heads);
+void test_dv_kernel_fp16(const fmha_fp16_t* P, const fmha_fp16_t* dO, fmha_fp16_t* dV,
+                         int M, int N, int K_dim, int total_heads);
 
 /* ---- exported by both libraries ---------------------------------------- */
 

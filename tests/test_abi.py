@@ -144,3 +144,38 @@ def test_delta_entry_requires_rowsum(kind, fn):
     f.restype = ctypes.c_int
     good = [0x10000 * (i + 1) for i in range(8)]
     assert f(*good, None, 128, 128, 64, 2, None) == 1
+
+
+STAGE_HOOKS = ["dp", "softmax_bwd", "dq", "dk", "dv"]
+
+
+@pytest.mark.parametrize("kind", ["bf16", "fp16"])
+@pytest.mark.parametrize("stage", STAGE_HOOKS)
+def test_stage_hooks_reject_bad_arguments_without_gpu(kind, stage):
+    """Every stage hook checks its arguments on the host before any CUDA call
+    and reports through fmha_bwd_last_error()."""
+    _ensure_built()
+    lib = ctypes.CDLL(LIBS[kind])
+    lib.fmha_bwd_last_error.restype = ctypes.c_int
+    lib.fmha_bwd_last_error_message.restype = ctypes.c_char_p
+    f = getattr(lib, f"test_{stage}_kernel" + ("_fp16" if kind == "fp16" else ""))
+    nints = 3 if stage == "softmax_bwd" else 4
+    f.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * nints
+    f.restype = None
+    good = [0x10000 * (i + 1) for i in range(3)]  # never dereferenced: rejected first
+
+    def call(ptrs, M, N, d, H):
+        ints = (M, N, H) if stage == "softmax_bwd" else (M, N, d, H)
+        f(*ptrs, *ints)
+        return lib.fmha_bwd_last_error(), lib.fmha_bwd_last_error_message().decode()
+
+    code, msg = call([None] + good[1:], 128, 128, 64, 2)
+    assert code == 1 and "null" in msg
+    assert call(good, 0, 128, 64, 2)[0] == 1
+    assert call(good, 128, 128, 64, 0)[0] == 1
+    assert call(good, 128, 130, 64, 2)[0] == 2
+    code, msg = call([p + 2 for p in good], 128, 128, 64, 2)
+    assert code == 2 and "aligned" in msg
+    if stage != "softmax_bwd":
+        code, msg = call(good, 128, 128, 96, 2)
+        assert code == 1 and "K_dim" in msg
