@@ -5,6 +5,7 @@
 #include "fmha_bwd_common_abi.cuh"
 #include "fmha_bwd_launch.cuh"
 #include "fmha_bwd_stages.cuh"
+#include "fmha_bwd_lse.cuh"
 
 using bf16 = __nv_bfloat16;
 
@@ -136,6 +137,15 @@ FMHA_API int fmha_bwd_full_noalloc(bf16* dQ, bf16* dK, bf16* dV, const bf16* Q, 
     return set_error(kErrDeviceTimeout, "in-kernel wait gave up (code %d, site %d, block %d)",
                      st.code, st.where, st.block);
   return set_error(kOk, "");
+}
+
+// ---- recompute-P entry: P = exp(scale Q K^T - LSE) is formed on chip; D =
+// rowsum(dO * O). Stream-ordered; returns 0 or an error code.
+FMHA_API int fmha_bwd_full_lse(bf16* dQ, bf16* dK, bf16* dV, const bf16* Q, const bf16* K, const bf16* V,
+                      const bf16* O, const bf16* dO, const float* LSE, int M, int N, int K_dim,
+                      int total_heads, float softmax_scale, cudaStream_t stream) {
+  return fmha_sm100::run_backward_lse<bf16>(dQ, dK, dV, Q, K, V, O, dO, LSE, M, N, K_dim, total_heads,
+                                          softmax_scale, stream);
 }
 
 // ---- stage hooks (replace the reference's test_* wrappers, src/fmha_bwd_kernels.hip:525-560).

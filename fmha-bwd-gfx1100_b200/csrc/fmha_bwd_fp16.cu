@@ -5,6 +5,7 @@
 #include "fmha_bwd_common_abi.cuh"
 #include "fmha_bwd_launch.cuh"
 #include "fmha_bwd_stages.cuh"
+#include "fmha_bwd_lse.cuh"
 
 using fp16 = __half;
 
@@ -35,6 +36,15 @@ FMHA_API int fmha_bwd_full_fp16_stream_events(fp16* dQ, fp16* dK, fp16* dV, cons
                              int total_heads, cudaStream_t stream, cudaEvent_t const* events) {
   return fmha_sm100::run_backward<fp16>(dQ, dK, dV, Q, K, V, P, dO, M, N, K_dim, total_heads,
                                         stream, /*sync=*/false, events);
+}
+
+// ---- recompute-P entry: P = exp(scale Q K^T - LSE) is formed on chip; D =
+// rowsum(dO * O). Stream-ordered; returns 0 or an error code.
+FMHA_API int fmha_bwd_full_fp16_lse(fp16* dQ, fp16* dK, fp16* dV, const fp16* Q, const fp16* K, const fp16* V,
+                      const fp16* O, const fp16* dO, const float* LSE, int M, int N, int K_dim,
+                      int total_heads, float softmax_scale, cudaStream_t stream) {
+  return fmha_sm100::run_backward_lse<fp16>(dQ, dK, dV, Q, K, V, O, dO, LSE, M, N, K_dim, total_heads,
+                                          softmax_scale, stream);
 }
 
 // ---- stage hooks (replace the reference's test_* wrappers, src/fmha_bwd_kernels_fp16.hip:284-314; C++ linkage there,

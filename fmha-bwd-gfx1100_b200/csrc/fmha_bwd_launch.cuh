@@ -221,9 +221,11 @@ inline KernelStatus read_status(const KernelStatus* p) {
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Validates the call. Returns kOk or an error code (already recorded).
+// `p_rows`: the call reads an [M][N] 16-bit P, whose rows must start on
+// 16-byte boundaries (N % 8 == 0); the recompute-P entries pass false.
 inline int check_args(const void* dQ, const void* dK, const void* dV, const void* Q,
                       const void* K, const void* V, const void* P, const void* dO, int M,
-                      int N, int D, int H) {
+                      int N, int D, int H, bool p_rows = true) {
   if (!dQ || !dK || !dV || !Q || !K || !V || !P || !dO)
     return set_error(kErrInvalidArgument, "null pointer argument");
   if (M <= 0 || N <= 0 || H <= 0 || D <= 0)
@@ -232,7 +234,7 @@ inline int check_args(const void* dQ, const void* dK, const void* dV, const void
   if (D != 64 && D != 128)
     return set_error(kErrInvalidArgument, "K_dim=%d unsupported (64 or 128)", D);
   if (H > 65535) return set_error(kErrInvalidArgument, "total_heads=%d exceeds 65535", H);
-  if (N % 8 != 0)
+  if (p_rows && N % 8 != 0)
     return set_error(kErrMisaligned, "N=%d: P rows must be a multiple of 16 bytes (N %% 8 == 0)", N);
   if (!aligned16(dQ) || !aligned16(dK) || !aligned16(dV) || !aligned16(Q) || !aligned16(K) ||
       !aligned16(V) || !aligned16(P) || !aligned16(dO))

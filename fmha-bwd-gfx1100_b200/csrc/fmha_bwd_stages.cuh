@@ -19,7 +19,7 @@
 // dS on chip. They exist for stage-level testing and debugging.
 #pragma once
 
-#include "fmha_bwd_kernels.cuh"
+#include "fmha_bwd_launch.cuh"
 
 namespace fmha_sm100 {
 

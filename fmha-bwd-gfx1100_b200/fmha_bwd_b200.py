@@ -42,6 +42,12 @@ DELTA_NAMES = {
     torch.float16: "fmha_bwd_full_fp16_delta",
 }
 
+# recompute-P entries: P = exp(scale Q K^T - LSE) formed on chip
+LSE_NAMES = {
+    torch.bfloat16: "fmha_bwd_full_lse",
+    torch.float16: "fmha_bwd_full_fp16_lse",
+}
+
 ERROR_NAMES = {
     0: "OK",
     1: "INVALID_ARGUMENT",
@@ -91,6 +97,10 @@ def load_library(dtype: torch.dtype = torch.bfloat16) -> ctypes.CDLL:
     delta = DELTA_NAMES[dtype]
     getattr(lib, delta).argtypes = _PTR_ARGS + [ctypes.c_void_p] + _INT_ARGS + [ctypes.c_void_p]
     getattr(lib, delta).restype = ctypes.c_int
+    lse = LSE_NAMES[dtype]
+    getattr(lib, lse).argtypes = (_PTR_ARGS + [ctypes.c_void_p] + _INT_ARGS +
+                                  [ctypes.c_float, ctypes.c_void_p])
+    getattr(lib, lse).restype = ctypes.c_int
     lib.fmha_bwd_last_error.argtypes = []
     lib.fmha_bwd_last_error.restype = ctypes.c_int
     lib.fmha_bwd_last_error_message.argtypes = []
@@ -182,6 +192,42 @@ def fmha_bwd(Q, K, V, P, dO, *, out=None, stream=None, sync: bool = True, delta=
         s = stream if stream is not None else torch.cuda.current_stream(Q.device)
         rc = getattr(lib, stream_fn)(*args, ctypes.c_void_p(s.cuda_stream))
         _raise_if_error(lib, rc)
+    return dQ, dK, dV
+
+
+def fmha_bwd_lse(Q, K, V, O, dO, LSE, scale: float, *, out=None, stream=None,
+                 sync: bool = True):
+    """Backward that recomputes P = exp(scale Q K^T - LSE) on chip instead of
+    reading it (the FlashAttention form). Q, O, dO: [H, M, d]; K, V: [H, N, d];
+    LSE: fp32 [H, M] (natural log of the row sums of exp(scale Q K^T)).
+    Returns (dQ, dK, dV) = (scale dS K, scale dS^T Q, P^T dO) with
+    dS = P (dO V^T - rowsum(dO * O)). Stream-ordered on ``stream`` (default:
+    torch's current stream); with ``sync`` the call waits and raises on an
+    in-kernel wait timeout."""
+    for name, t in (("Q", Q), ("K", K), ("V", V), ("O", O), ("dO", dO)):
+        if not t.is_cuda or not t.is_contiguous() or t.dtype != Q.dtype:
+            raise ValueError(f"{name} must be a contiguous CUDA tensor of {Q.dtype}")
+    d = Q.shape[-1]
+    M, N = Q.shape[-2], K.shape[-2]
+    H = Q.shape[:-2].numel()
+    if K.shape[-1] != d or V.shape != K.shape or O.shape != Q.shape or dO.shape != Q.shape:
+        raise ValueError("shape mismatch among Q, K, V, O, dO")
+    if not LSE.is_cuda or LSE.dtype != torch.float32 or not LSE.is_contiguous() or LSE.numel() != H * M:
+        raise ValueError("LSE must be a contiguous fp32 CUDA tensor of H*M elements")
+    lib = load_library(Q.dtype)
+    if out is None:
+        out = (torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V))
+    dQ, dK, dV = out
+    s = stream if stream is not None else torch.cuda.current_stream(Q.device)
+    rc = getattr(lib, LSE_NAMES[Q.dtype])(
+        dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), Q.data_ptr(), K.data_ptr(), V.data_ptr(),
+        O.data_ptr(), dO.data_ptr(), LSE.data_ptr(), M, N, d, H, float(scale),
+        ctypes.c_void_p(s.cuda_stream))
+    _raise_if_error(lib, rc)
+    if sync:
+        s.synchronize()
+        if lib.fmha_bwd_poll_device_status() != 0:
+            raise FmhaBwdError(6, "fmha_bwd_lse: an in-kernel wait gave up")
     return dQ, dK, dV
 
 

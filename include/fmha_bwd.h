@@ -97,6 +97,25 @@ int fmha_bwd_full_delta(fmha_bf16_t* dQ, fmha_bf16_t* dK, fmha_bf16_t* dV,
                         const fmha_bf16_t* dO, const float* Dsum, int M, int N,
                         int K_dim, int total_heads, fmha_stream_t stream);
 
+/* Recompute-P variant (the reference's path reads a materialised P; this is
+ * the "produce P on the fly from Q, K and the row log-sum-exp" extension, no
+ * reference counterpart). Per head: O [M][K_dim] is the forward output and
+ * LSE [M] (fp32, 4-byte aligned) holds log sum_n exp(softmax_scale Q_m.K_n).
+ * The kernels form P = exp(softmax_scale Q K^T - LSE) on chip and return the
+ * gradients of the scaled-score attention:
+ *   D = rowsum(dO * O), dS = P * (dO V^T - D),
+ *   dQ = softmax_scale dS K, dK = softmax_scale dS^T Q, dV = P^T dO.
+ * With softmax_scale = 1 and O = P V this equals fmha_bwd_full_py on that P,
+ * with no M x N buffer anywhere. N needs no alignment (no P rows are read);
+ * other preconditions as fmha_bwd_full_py; softmax_scale > 0 and finite.
+ * Stream-ordered; returns 0 or an error code. */
+int fmha_bwd_full_lse(fmha_bf16_t* dQ, fmha_bf16_t* dK, fmha_bf16_t* dV,
+                      const fmha_bf16_t* Q, const fmha_bf16_t* K,
+                      const fmha_bf16_t* V, const fmha_bf16_t* O,
+                      const fmha_bf16_t* dO, const float* LSE, int M, int N,
+                      int K_dim, int total_heads, float softmax_scale,
+                      fmha_stream_t stream);
+
 /* No counterpart in the reference. Allocation-free variant of
  * fmha_bwd_full_stream: the fp32 rowsum scratch D (total_heads * M floats)
  * and the wait-status slot live in file-scope __device__ arrays of the
@@ -168,6 +187,14 @@ int fmha_bwd_full_fp16_delta(fmha_fp16_t* dQ, fmha_fp16_t* dK, fmha_fp16_t* dV,
                              const fmha_fp16_t* dO, const float* Dsum, int M,
                              int N, int K_dim, int total_heads,
                              fmha_stream_t stream);
+
+/* fp16 recompute-P variant, as fmha_bwd_full_lse. */
+int fmha_bwd_full_fp16_lse(fmha_fp16_t* dQ, fmha_fp16_t* dK, fmha_fp16_t* dV,
+                           const fmha_fp16_t* Q, const fmha_fp16_t* K,
+                           const fmha_fp16_t* V, const fmha_fp16_t* O,
+                           const fmha_fp16_t* dO, const float* LSE, int M, int N,
+                           int K_dim, int total_heads, float softmax_scale,
+                           fmha_stream_t stream);
 
 /* fp16 profiling variant, as fmha_bwd_full_stream_events. */
 int fmha_bwd_full_fp16_stream_events(fmha_fp16_t* dQ, fmha_fp16_t* dK,

@@ -179,3 +179,23 @@ def test_stage_hooks_reject_bad_arguments_without_gpu(kind, stage):
     if stage != "softmax_bwd":
         code, msg = call(good, 128, 128, 96, 2)
         assert code == 1 and "K_dim" in msg
+
+
+@pytest.mark.parametrize("kind,fn", [("bf16", "fmha_bwd_full_lse"), ("fp16", "fmha_bwd_full_fp16_lse")])
+def test_lse_entry_rejects_bad_arguments_without_gpu(kind, fn):
+    """The recompute-P entry checks LSE, the scale and the usual sizes on the
+    host; N needs no alignment there (no P rows are read)."""
+    _ensure_built()
+    lib = ctypes.CDLL(LIBS[kind])
+    lib.fmha_bwd_last_error_message.restype = ctypes.c_char_p
+    f = getattr(lib, fn)
+    f.argtypes = [ctypes.c_void_p] * 9 + [ctypes.c_int] * 4 + [ctypes.c_float, ctypes.c_void_p]
+    f.restype = ctypes.c_int
+    good = [0x10000 * (i + 1) for i in range(8)]
+    lse = 0x90000
+    assert f(*good, None, 128, 128, 64, 2, 1.0, None) == 1          # null LSE
+    assert f(*good, lse + 2, 128, 128, 64, 2, 1.0, None) == 2       # misaligned LSE
+    assert f(*good, lse, 128, 128, 64, 2, 0.0, None) == 1           # scale must be > 0
+    assert f(*good, lse, 128, 128, 64, 2, float("nan"), None) == 1
+    assert f(*good, lse, 128, 128, 96, 2, 1.0, None) == 1           # K_dim
+    assert f(None, *good[1:], lse, 128, 128, 64, 2, 1.0, None) == 1
