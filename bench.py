@@ -24,6 +24,8 @@ Reported (one JSON line from rank 0):
               CUDA-event duration, against the measured bf16 peak
   cpu_baseline  the reference's own CPU backward (cpu_reference.hpp), timed
               on this host's cores on a bounded sample (rank 0, N=1 only)
+  recompute_p   the same workload through fmha_bwd_full_lse (P formed on chip
+              from the forward's LSE and O), after the timed region
 
 --impl reference times the reference's CPU implementation of the path (the
 reference's GPU code is HIP for gfx1100 and cannot run here) on the same
@@ -228,6 +230,9 @@ def main() -> int:
     ap.add_argument("--cpu-rows", type=int, default=2048,
                     help="query rows per head in the CPU baseline sample (0: all M rows); "
                          "2048 rows of 16 FLUX heads take about 15 s on 16 host cores")
+    ap.add_argument("--lse-steps", type=int, default=200,
+                    help="timed steps of the recompute-P entry (fmha_bwd_full_lse) on the "
+                         "same workload, reported under 'recompute_p' (0: skip)")
     ap.add_argument("--cpu-rows-per-step", type=int, default=0,
                     help="query rows per head per step of the reference arm "
                          "(0: sized so the run takes about two minutes)")
@@ -385,6 +390,59 @@ def main() -> int:
         if not torch.equal(dK2, dK) or not torch.equal(dV2, dV):
             raise RuntimeError("e2e outputs differ from the device-resident run")
 
+    # ---- the recompute-P entry on the same workload: P = exp(scale Q K^T - LSE)
+    # formed on chip from the forward's LSE and O (scale = 1/sqrt(d), the
+    # scale the synthetic P was made with), 14*M*N*d of MMA work per head.
+    recompute_p = None
+    if args.lse_steps > 0:
+        import math
+
+        scale = 1.0 / math.sqrt(w.d)
+        LSE = torch.empty(heads, w.M, device=dev, dtype=torch.float32)
+        Ofwd = torch.empty_like(Q)
+        for h in range(heads):
+            S = (Q[h].float() @ K[h].float().T) * scale
+            LSE[h] = torch.logsumexp(S, dim=-1)
+            Ofwd[h] = (torch.exp(S - LSE[h][:, None]) @ V[h].float()).to(Q.dtype)
+            del S
+        lse_out = (torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V))
+
+        def lse_step():
+            F.fmha_bwd_lse(Q, K, V, Ofwd, dO, LSE, scale, out=lse_out, stream=stream, sync=False)
+
+        for _ in range(args.warmup):
+            lse_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        l0 = torch.cuda.Event(enable_timing=True)
+        l1 = torch.cuda.Event(enable_timing=True)
+        l0.record(stream)
+        for _ in range(args.lse_steps):
+            lse_step()
+        l1.record(stream)
+        torch.cuda.synchronize(dev)
+        lse_ms = l0.elapsed_time(l1)
+        if lib.fmha_bwd_poll_device_status() != 0:
+            raise RuntimeError("device status reported a wait timeout in the recompute-P run")
+        if world > 1:
+            t = torch.tensor([lse_ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            lse_ms = float(t.item())
+        # dV = P^T dO does not depend on D: it must agree with the P-reading run
+        rel = float((lse_out[2].float() - dV.float()).norm() / dV.float().norm().clamp_min(1e-30))
+        if not rel < 2e-2:
+            raise RuntimeError(f"recompute-P dV differs from the P-reading run (rel-L2 {rel:.3g})")
+        recompute_p = {
+            "entry": "fmha_bwd_full_lse" if w.dtype == "bf16" else "fmha_bwd_full_fp16_lse",
+            "value": flops_rank * world * args.lse_steps / (lse_ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s (same counted 8*M*N*d per head)",
+            "ms_per_step": lse_ms / args.lse_steps, "steps": args.lse_steps,
+            "mma_work_per_head": "14*M*N*d (adds S = Q K^T in both kernels; reads no P)",
+            "dV_rel_l2_vs_P_path": rel,
+        }
+        del LSE, Ofwd, lse_out
+
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -419,6 +477,7 @@ def main() -> int:
                    "parallelism": f"head-sharded x{world}, no data-path collective",
                    "l2": "inputs larger than L2 (P is 1.02 GB per GPU vs 126 MB L2); no flush"},
         "e2e": e2e,
+        "recompute_p": recompute_p,
         "gpu_launches": 2 * K_steps,
         "roofline": roofline,
         "clocks": clocks,
