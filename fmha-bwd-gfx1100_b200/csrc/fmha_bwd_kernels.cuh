@@ -21,10 +21,13 @@
 //      writes dQ (16-bit) and D (fp32) directly.
 //
 //   2. dkv_kernel  one CTA per (128-column key tile j, head). V_j stays in
-//      shared memory. For every query tile i it computes dP_ij (TMEM),
-//      dS_ij = P (dP - D_i) in registers (stored once to shared memory as
-//      16-bit), and accumulates dV_j += P^T dO_i and dK_j += dS^T Q_i in
-//      TMEM. dP and dS never reach global memory.
+//      shared memory. For every query tile i it computes dP_ij^T (TMEM, key
+//      index on the lanes), dS_ij^T = P^T (dP^T - D_i) in registers, written
+//      back into TMEM as 16-bit, and accumulates dV_j += P^T dO_i and
+//      dK_j += dS^T Q_i (A operand from TMEM) in TMEM. dP and dS never reach
+//      global memory.
+//
+// Both kernels are persistent (one CTA per SM walking the work items).
 //
 // Shared-memory tiles are loaded by TMA with 128-byte swizzle as boxes of
 // 64 columns x 128 rows (16 KB). A [128][128] tile is two boxes side by side

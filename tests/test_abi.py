@@ -121,6 +121,13 @@ def test_python_mirror_fails_loudly_without_cuda_tensors():
         F.fmha_bwd(x, x, x, torch.zeros(1, 128, 128, dtype=torch.bfloat16), x)
     with pytest.raises(TypeError):
         F.library_path(torch.float32)
+    # the stage hooks and the recompute-P entry check their tensors the same way
+    with pytest.raises(ValueError):
+        F.run_stage("dp", x, x)
+    with pytest.raises(ValueError):
+        F.run_stage("no_such_stage", x, x)
+    with pytest.raises(ValueError):
+        F.fmha_bwd_lse(x, x, x, x, x, torch.zeros(1, 128), 0.125)
 
 
 @pytest.mark.parametrize("kind", ["bf16", "fp16"])
