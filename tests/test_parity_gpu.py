@@ -275,3 +275,27 @@ def test_precomputed_rowsum_entry(F, oracle_built, M, N, d, H, dtype):
         ref = O.oracle_bwd(*bits, name)
         for nm, got, r in zip(("dQ", "dK", "dV"), b, ref[:3]):
             _assert_ok(O, nm, _f32(got), r, name)
+
+
+@pytest.mark.parametrize("M,N,d,H,name", [(1, 8, 64, 65535, "bf16"), (3, 16, 64, 65535, "fp16"),
+                                          (1, 16384, 128, 3, "bf16"), (16384, 8, 64, 2, "fp16")])
+def test_extreme_shapes(F, oracle_built, M, N, d, H, name):
+    """The limits the ABI accepts: the maximum head count (65535 work items
+    per kernel walked by the persistent CTAs), one query row against 16384
+    keys, 16384 query rows against one 8-key tile. Every head against the
+    fp32 GPU recompute; the first and last heads against the CPU oracle."""
+    O = oracle_built
+    dt = _dt(name)
+    g = torch.Generator(device="cuda").manual_seed(71)
+    Q, K, V, dO = (torch.randn(H, r, d, device="cuda", generator=g).to(dt) for r in (M, N, N, M))
+    P = torch.softmax(torch.randn(H, M, N, device="cuda", generator=g) * 2.0, dim=-1).to(dt)
+    dQ, dK, dV = F.fmha_bwd(Q, K, V, P, dO)
+    torch.cuda.synchronize()
+    rq, rk, rv = _torch_reference(Q, K, V, P, dO)
+    for label, got, ref in (("dQ", dQ, rq), ("dK", dK, rk), ("dV", dV, rv)):
+        _assert_ok(O, label, _f32(got), ref.cpu().numpy(), name)
+    for h in (0, H - 1):
+        sl = slice(h, h + 1)
+        ref = O.oracle_bwd(*(_to_bits(t[sl]) for t in (Q, K, V, P, dO)), name)
+        for label, got, r in zip(("dQ", "dK", "dV"), (dQ[sl], dK[sl], dV[sl]), ref[:3]):
+            _assert_ok(O, label, _f32(got), r, name)
