@@ -19,9 +19,18 @@ Reported (one JSON line from rank 0):
               (fmha_bwd_full_py) with host buffers: pinned-host -> device
               copies of Q, K, V, P, dO and device -> host copies of dQ, dK, dV
               inside the timed region, every step
-  roofline    the dominant kernel (dkv_kernel: dP, dV, dK = 6*M*N*d per head
-              of the algorithm's 8*M*N*d): its FLOPs per launch / its mean
-              CUDA-event duration, against the measured bf16 peak
+  roofline    the backward call (dq_kernel + dkv_kernel) against the
+              tensor roofline: achieved = the algorithm's 8*M*N*d*heads
+              FLOPs per call / ms_per_step, frac = achieved / the measured
+              bf16 peak; traffic = both kernels' DRAM bytes per call (ncu),
+              with its ratio to the algorithmic bytes; each kernel's own MMA
+              work (6*M*N*d per head) and time under "kernels"
+  strong      strong scaling on the long video workload (M=N=16384, d=128,
+              40 heads): the 40 heads are split over the N ranks by
+              workloads.head_range (40/20/10/5 heads per GPU at N=1/2/4/8),
+              P generated per head on the device; per-rank and
+              max-over-ranks ms, TFLOP/s and the fraction of the one-GPU
+              roofline time
   cpu_baseline  the reference's own CPU backward (cpu_reference.hpp), timed
               on this host's cores on a bounded sample (rank 0, N=1 only)
   recompute_p   the same workload through fmha_bwd_full_lse (P formed on chip
@@ -233,6 +242,9 @@ def main() -> int:
     ap.add_argument("--lse-steps", type=int, default=200,
                     help="timed steps of the recompute-P entry (fmha_bwd_full_lse) on the "
                          "same workload, reported under 'recompute_p' (0: skip)")
+    ap.add_argument("--strong-steps", type=int, default=5,
+                    help="timed steps of the strong-scaling run on the video workload "
+                         "(40 heads split over the ranks; 0: skip)")
     ap.add_argument("--cpu-rows-per-step", type=int, default=0,
                     help="query rows per head per step of the reference arm "
                          "(0: sized so the run takes about two minutes)")
@@ -379,16 +391,92 @@ def main() -> int:
         e2e_ms = s0.elapsed_time(s1)
         if lib.fmha_bwd_last_error() != 0:
             raise RuntimeError(lib.fmha_bwd_last_error_message().decode())
+        # the host->device copies alone: this rank's pinned-host copy rate
+        c0 = torch.cuda.Event(enable_timing=True)
+        c1 = torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for _ in range(3):
+            for dst, src in zip(dev_in, (hQ, hK, hV, hP, hdO)):
+                dst.copy_(src, non_blocking=True)
+        c1.record()
+        torch.cuda.synchronize(dev)
+        h2d_gbs = 3.0 * h2d / (c0.elapsed_time(c1) * 1e-3) / 1e9
         if world > 1:
-            t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_ms = float(t.item())
+            st = workloads.gather_rank_stats(dist, [e2e_ms, h2d_gbs], dev)
+            e2e_ms = float(st[:, 0].max())
+            h2d_rank = [float(x) for x in st[:, 1]]
+        else:
+            h2d_rank = [h2d_gbs]
         e2e = {"value": flops_rank * world * args.e2e_steps / (e2e_ms * 1e-3) / 1e12,
                "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": e2e_ms / args.e2e_steps,
+               "h2d_gbs_per_rank": h2d_rank,
+               "note": "host copies dominate: every rank's pinned buffers sit in one host's "
+                       "memory, so the per-rank copy rate falls as ranks are added",
                "entry": "fmha_bwd_full_py" if w.dtype == "bf16" else "fmha_bwd_full_fp16"}
         if not torch.equal(dK2, dK) or not torch.equal(dV2, dV):
             raise RuntimeError("e2e outputs differ from the device-resident run")
+        del hQ, hK, hV, hP, hdO, ohQ, ohK, ohV, dQ2, dK2, dV2, dev_in
+
+    # ---- strong scaling: the long video workload's 40 heads split over the
+    # ranks (workloads.head_range: 40/20/10/5 heads per GPU at 1/2/4/8 GPUs),
+    # each rank generating its heads' inputs (P per head) on its own GPU
+    strong = None
+    if args.strong_steps > 0:
+        wv = workloads.WORKLOADS["video"]
+        h0, h1 = workloads.head_range(wv.heads, rank, world)
+        nh = h1 - h0
+        sstep = None
+        if nh > 0:
+            sQ, sK, sV, sP, sdO = workloads.make_inputs(wv, seed=42, device=dev, heads=nh,
+                                                       head_offset=h0)
+            so = (torch.empty_like(sQ), torch.empty_like(sK), torch.empty_like(sV))
+            sptrs = (so[0].data_ptr(), so[1].data_ptr(), so[2].data_ptr(), sQ.data_ptr(),
+                     sK.data_ptr(), sV.data_ptr(), sP.data_ptr(), sdO.data_ptr(), wv.M, wv.N,
+                     wv.d, nh)
+
+            def sstep():
+                rc = ev_fn(*sptrs, ctypes.c_void_p(stream.cuda_stream), None)
+                if rc != 0:
+                    raise F.FmhaBwdError(rc, lib.fmha_bwd_last_error_message().decode())
+
+            for _ in range(2):
+                sstep()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        if sstep is not None:
+            for _ in range(args.strong_steps):
+                sstep()
+        a1.record(stream)
+        torch.cuda.synchronize(dev)
+        if lib.fmha_bwd_poll_device_status() != 0:
+            raise RuntimeError("device status reported a wait timeout in the strong-scaling run")
+        ms_rank = a0.elapsed_time(a1) / args.strong_steps if sstep is not None else 0.0
+        if world > 1:
+            st = workloads.gather_rank_stats(dist, [ms_rank, nh], dev)
+            ms_ranks = [float(x) for x in st[:, 0]]
+            heads_ranks = [int(x) for x in st[:, 1]]
+        else:
+            ms_ranks, heads_ranks = [ms_rank], [nh]
+        s_ms = max(ms_ranks)
+        s_flops = wv.flops()
+        peaks_s, _ = load_peaks()
+        roof1_ms = s_flops / (float(peaks_s["bf16_tflops"]) * 1e12) * 1e3
+        strong = {
+            "workload": wv.description, "scaling": "strong", "total_heads": wv.heads,
+            "heads_per_rank": heads_ranks, "ms_per_step_per_rank": ms_ranks,
+            "ms_per_step": s_ms, "steps": args.strong_steps,
+            "value": s_flops / (s_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "one_gpu_roofline_ms": roof1_ms,
+            "frac_of_roofline": (roof1_ms / world) / s_ms,
+        }
+        if sstep is not None:
+            del sQ, sK, sV, sP, sdO, so
+        torch.cuda.empty_cache()
 
     # ---- the recompute-P entry on the same workload: P = exp(scale Q K^T - LSE)
     # formed on chip from the forward's LSE and O (scale = 1/sqrt(d), the
@@ -452,20 +540,39 @@ def main() -> int:
     peaks, peak_src = load_peaks()
     peak = float(peaks["bf16_tflops"])
     peak_sus = float(peaks.get("bf16_tflops_sustained", peak))
-    dkv_flops = 0.75 * flops_rank  # dP, dV, dK: 6 of the 8 M*N*d terms
-    achieved = dkv_flops / (main_ms * 1e-3) / 1e12
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    # the whole call (both kernels) against the tensor roofline: the
+    # algorithm's 8*M*N*d FLOPs per head over the measured time per step
+    achieved = flops_rank / (ms_per_step * 1e-3) / 1e12
     dq_ms = statistics.mean(t_dq)
-    traffic = load_traffic(f"dkv_kernel:{w.name}")
+    mma_flops = 0.75 * flops_rank  # each kernel issues 6*M*N*d of MMA work per head
+    t_dq_traffic = load_traffic(f"dq_kernel:{w.name}")
+    t_dkv_traffic = load_traffic(f"dkv_kernel:{w.name}")
+    traffic = (t_dq_traffic + t_dkv_traffic
+               if t_dq_traffic is not None and t_dkv_traffic is not None else None)
+    alg_bytes = w.algorithmic_bytes(heads)
     roofline = {
-        "kernel": "dkv_kernel (dP, dS, dV, dK; 6*M*N*d per head)",
+        "kernel": "backward call: dq_kernel + dkv_kernel (8*M*N*d per head counted)",
         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
         "frac": achieved / peak, "traffic": traffic,
+        "algorithmic_bytes": alg_bytes,
+        "traffic_over_algorithmic": traffic / alg_bytes if traffic else None,
+        "bytes_roof_ms": alg_bytes / (hbm * 1e9) * 1e3,
+        "flops_roof_ms": flops_rank / (peak * 1e12) * 1e3,
         "peak_source": f"{peak_src} (bf16 burst, MEASURED_PEAKS.json)" if peak_src == "measured"
         else "fallback 1.59 PFLOP/s",
         "frac_of_sustained": achieved / peak_sus,
-        "kernel_ms": {"dq_kernel": dq_ms, "dkv_kernel": main_ms},
-        "dq_kernel_frac": 0.75 * flops_rank / (dq_ms * 1e-3) / 1e12 / peak,
-        "step_frac_of_peak": value / world / peak,
+        "kernels": {
+            "dq_kernel": {"ms": dq_ms, "mma_tflops": mma_flops / (dq_ms * 1e-3) / 1e12,
+                          "mma_frac": mma_flops / (dq_ms * 1e-3) / 1e12 / peak,
+                          "traffic": t_dq_traffic},
+            "dkv_kernel": {"ms": main_ms, "mma_tflops": mma_flops / (main_ms * 1e-3) / 1e12,
+                           "mma_frac": mma_flops / (main_ms * 1e-3) / 1e12 / peak,
+                           "traffic": t_dkv_traffic},
+            "mma_work": "each kernel issues 6*M*N*d of MMA work per head (12 in all for the "
+                        "8 counted): dP in both, then B = P K and A = E K in dq_kernel, dV "
+                        "and dK in dkv_kernel",
+        },
     }
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
@@ -477,6 +584,7 @@ def main() -> int:
                    "parallelism": f"head-sharded x{world}, no data-path collective",
                    "l2": "inputs larger than L2 (P is 1.02 GB per GPU vs 126 MB L2); no flush"},
         "e2e": e2e,
+        "strong": strong,
         "recompute_p": recompute_p,
         "gpu_launches": 2 * K_steps,
         "roofline": roofline,

@@ -318,11 +318,26 @@ def pytorch_naive_backward(Q, K, V, P, dO):
     return dQ, dK, dV
 
 
+def _einsum_backward_native(Q, K, V, P, dO):
+    """The reference script's einsum backward (benchmark_pytorch_final.py:58-70)
+    in the inputs' own dtype, as that script times it (:110-115)."""
+    dP = torch.einsum("...mk,...nk->...mn", dO, V)
+    rowsum = (dP * P).sum(dim=-1, keepdim=True)
+    dS = P * (dP - rowsum)
+    dQ = torch.einsum("...mn,...nk->...mk", dS, K)
+    dK = torch.einsum("...mn,...mk->...nk", dS, Q)
+    dV = torch.einsum("...mn,...mk->...nk", P, dO)
+    return dQ, dK, dV
+
+
 def benchmark_size(batch, heads, M, N, K_dim, dtype=torch.bfloat16, warmup=5, reps=20):
     """Mirror of the reference's benchmark_size (benchmark_pytorch_final.py:82-136):
-    seeded inputs, warmup, CUDA-event timing of ``reps`` synchronous calls,
+    seeded inputs, warmup, CUDA-event timing of ``reps`` synchronous calls and
+    of ``reps`` einsum backwards in the inputs' dtype (the PyTorch baseline),
     FLOPs = 4 * 2*M*N*d per head (:125-127, here summed over batch*heads),
-    and the max difference against the einsum reference."""
+    and the max difference against the einsum reference (computed here in
+    fp32). Returns the reference's keys: M, N, K, custom_time_ms,
+    pytorch_time_ms, speedup, max_diff, custom_tflops."""
     device = torch.device("cuda")
     torch.manual_seed(42)
     Q = torch.randn(batch, heads, M, K_dim, dtype=dtype, device=device)
@@ -341,6 +356,15 @@ def benchmark_size(batch, heads, M, N, K_dim, dtype=torch.bfloat16, warmup=5, re
     end.record()
     torch.cuda.synchronize()
     custom_ms = start.elapsed_time(end) / reps
+    for _ in range(warmup):
+        _einsum_backward_native(Q, K, V, P, dO)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(reps):
+        _einsum_backward_native(Q, K, V, P, dO)
+    end.record()
+    torch.cuda.synchronize()
+    pt_ms = start.elapsed_time(end) / reps
     rQ, rK, rV = pytorch_naive_backward(Q, K, V, P, dO)
     max_diff = max((dQ.float() - rQ).abs().max().item(), (dK.float() - rK).abs().max().item(),
                    (dV.float() - rV).abs().max().item())
@@ -348,6 +372,8 @@ def benchmark_size(batch, heads, M, N, K_dim, dtype=torch.bfloat16, warmup=5, re
     return {
         "M": M, "N": N, "K": K_dim,
         "custom_time_ms": custom_ms,
+        "pytorch_time_ms": pt_ms,
+        "speedup": pt_ms / custom_ms if custom_ms > 0 else 0.0,
         "max_diff": max_diff,
         "custom_tflops": flops / (custom_ms * 1e-3) / 1e12 if custom_ms > 0 else 0.0,
     }

@@ -135,19 +135,20 @@ def test_full_size_workloads(F, oracle_built, wname):
 
 
 def test_long_sequence_64bit_offsets(F, oracle_built):
-    """The long video shape (M = N = 16384, d = 128) with 10 heads: the last
-    head's P starts 2.4e9 elements in, past 2^31, so every per-head offset
-    must be 64-bit (the reference's int products overflow here). First and
-    last heads against the fp32 GPU recompute."""
+    """The whole long video workload (M = N = 16384, d = 128, 40 heads, P =
+    21.5 GB): h*M*N reaches 1.07e10, far past 2^31, so every per-head offset
+    must be 64-bit (the reference's int products overflow here,
+    src/fmha_bwd_kernels.hip:72-74 and :480-481). The first, a middle and the
+    last head against the fp32 GPU recompute."""
     import workloads
 
     O = oracle_built
-    w = workloads.Workload("video10", 16384, 16384, 128, 10, "bf16")
-    assert (w.heads - 1) * w.M * w.N > 2**31
+    w = workloads.WORKLOADS["video"]
+    assert w.heads == 40 and (w.heads - 1) * w.M * w.N > 2**33
     Q, K, V, P, dO = workloads.make_inputs(w, seed=7)
     dQ, dK, dV = F.fmha_bwd(Q, K, V, P, dO)
     torch.cuda.synchronize()
-    for h in (0, w.heads - 1):
+    for h in (0, w.heads // 2, w.heads - 1):
         sl = slice(h, h + 1)
         rq, rk, rv = _torch_reference(Q[sl], K[sl], V[sl], P[sl], dO[sl])
         _assert_ok(O, "dQ", _f32(dQ[sl]), rq.cpu().numpy(), "bf16")
