@@ -158,8 +158,12 @@ struct DqCfg {
   static constexpr int kSmemBytes = kOffBar + kBarBytes + 1024;
   static constexpr int kEpiWarps = 8;
   static constexpr int kFirstEpiWarp = 2;
-  static constexpr int kAbWarp = kFirstEpiWarp + kEpiWarps;  // second MMA issuer
-  static constexpr int kThreads = 32 * (kAbWarp + 1);
+  // D = 64: B and A have an issuing thread each (kBWarp, kAWarp); D = 128:
+  // kBWarp issues both (at D = 128 the split measured slower).
+  static constexpr bool kSplit = D == 64;
+  static constexpr int kBWarp = kFirstEpiWarp + kEpiWarps;  // MMA issuer of B (and A)
+  static constexpr int kAWarp = kBWarp + 1;                   // MMA issuer of A (D = 64)
+  static constexpr int kThreads = 32 * (kBWarp + 1 + (kSplit ? 1 : 0));
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kColX = 0;  // + 128 * buffer
   static constexpr uint32_t kColA = 256;
@@ -173,19 +177,20 @@ enum DqBar : int {
   kQbVFull0 = 1,    // + slot (up to 3)
   kQbVEmpty0 = 4,   // + slot
   kQbKFull0 = 7,    // + slot
-  kQbKEmpty0 = 10,  // + slot
+  kQbKEmpty0 = 10,  // + slot: commits of B_j and A_j
   kQbPFull0 = 13,   // + slot
   kQbPEmpty0 = 16,  // + slot: MMA commit after B_j + 8 epilogue warps
   kQbXFull0 = 19,   // + buffer (2)
   kQbEFull0 = 21,   // + buffer
   kQbXFree0 = 23,   // + buffer
-  kQbAB = 25,       // A and B of an item complete
+  kQbAB = 25,       // A and B of an item complete (a commit from each issuer)
   kQbDrain = 26,
   kQbXch0 = 27,     // + lane quarter (4): the two warps of a quarter swap values
   kQbDrain2 = 31,   // drain of the second MMA issuer
   kQbDOEmpty = 32,  // the dP MMAs of an item are done with dO_i
   kQbAccEmpty = 33, // the dS warps have read an item's A and B (8 warps)
-  kNumDqBars = 34,
+  kQbDrain3 = 34,   // drain of the third MMA issuer
+  kNumDqBars = 35,
 };
 static_assert(kNumDqBars * 8 + 8 <= 512, "dq barrier area");
 
@@ -224,7 +229,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
     }
     for (int s = 0; s < SK; ++s) {
       mbar_init(&bar[kQbKFull0 + s], 1);
-      mbar_init(&bar[kQbKEmpty0 + s], 1);
+      mbar_init(&bar[kQbKEmpty0 + s], (Cfg::kSplit && !kGivenD) ? 2 : 1);
     }
     for (int s = 0; s < SP; ++s) {
       mbar_init(&bar[kQbPFull0 + s], 1);
@@ -235,10 +240,11 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       mbar_init(&bar[kQbEFull0 + b], Cfg::kEpiWarps);
       mbar_init(&bar[kQbXFree0 + b], 1);
     }
-    mbar_init(&bar[kQbAB], 1);
+    mbar_init(&bar[kQbAB], (Cfg::kSplit && !kGivenD) ? 2 : 1);
     mbar_init(&bar[kQbAccEmpty], Cfg::kEpiWarps);
     mbar_init(&bar[kQbDrain], 1);
     mbar_init(&bar[kQbDrain2], 1);
+    mbar_init(&bar[kQbDrain3], 1);
     for (int q = 0; q < 4; ++q) mbar_init(&bar[kQbXch0 + q], 2);
     *abort_flag = 0;
     fence_mbar_init();
@@ -327,13 +333,15 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
           mbar_wait_drain(&bar[kQbKFull0 + j % SK], (j / SK) & 1, timeout_ns);
       }
     }
-  } else if (warp == 1 || warp == Cfg::kAbWarp) {
-    // ---- Two MMA issuers. The tensor pipe accepts only about one
-    // instruction ahead of the one executing, so a single issuing thread
-    // leaves it idle at every wait; with two, one keeps it fed while the
-    // other waits. Warp 1: dP_j = dO_i V_j^T into X_(g%2). Warp kAbWarp:
-    // B_j += P_ij K_j, then A_j += E_ij K_j (E from TMEM); it starts an item
-    // once the dS warps have read the previous item's A and B.
+  } else if (warp == 1 || warp == Cfg::kBWarp || warp == Cfg::kAWarp) {
+    // ---- MMA issuers. The tensor pipe accepts only about one instruction
+    // ahead of the one executing, and a thread between two of its MMA groups
+    // spends a few hundred cycles on barrier waits and commits, so the work
+    // is spread over several issuing threads that keep the pipe fed while one
+    // waits. Warp 1: dP_j = dO_i V_j^T into X_(g%2). Warp kBWarp:
+    // B_j += P_ij K_j, and at D = 128 then A_j += E_ij K_j (E from TMEM); at
+    // D = 64 warp kAWarp issues A_j. B and A start an item once the epilogue
+    // has read the previous item's A and B.
     if (lane == 0) {
       constexpr bool kB = Elem<T>::kBF16;
       // dP = dO_i V_j^T: A = dO_i (K-major over d), B = V_j (K-major over d)
@@ -369,7 +377,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
           umma_commit(&bar[kQbDrain]);
           mbar_wait_drain(&bar[kQbDrain], 0, timeout_ns);
         }
-      } else {
+      } else if (warp == Cfg::kBWarp && !Cfg::kSplit) {
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
           if (tc > 0 && !mbar_wait(&bar[kQbAccEmpty], (tc - 1) & 1, ctx, 16)) { ok = false; break; }
           for (int j = 0; j < nt; ++j, ++g) {
@@ -404,6 +412,56 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
         if (!ok) {
           umma_commit(&bar[kQbDrain2]);
           mbar_wait_drain(&bar[kQbDrain2], 0, timeout_ns);
+        }
+      } else if (warp == Cfg::kBWarp) {
+        if constexpr (!kGivenD) {
+          for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+            if (tc > 0 && !mbar_wait(&bar[kQbAccEmpty], (tc - 1) & 1, ctx, 16)) { ok = false; break; }
+            for (int j = 0; j < nt; ++j, ++g) {
+              if (!mbar_wait(&bar[kQbPFull0 + g % SP], (g / SP) & 1, ctx, 14)) { ok = false; break; }
+              if (!mbar_wait(&bar[kQbKFull0 + g % SK], (g / SK) & 1, ctx, 15)) { ok = false; break; }
+              tc_fence_after();
+              const uint64_t dK = make_sw128_desc(sK0 + (g % SK) * Cfg::kMD, kBoxBytes, 1024);
+              const uint64_t dP = make_sw128_desc(sP0 + (g % SP) * Cfg::kPT, 16, 1024);
+#pragma unroll
+              for (int k = 0; k < kTile / 16; ++k) {
+                umma_f16_ss(tmem + Cfg::kColB, desc_advance(dP, (k >> 2) * kBoxBytes + (k & 3) * 32),
+                            desc_advance(dK, k * 2048), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+              }
+              umma_commit(&bar[kQbPEmpty0 + g % SP]);  // the tensor core's read of P_ij
+              umma_commit(&bar[kQbKEmpty0 + g % SK]);
+            }
+            if (ok) umma_commit(&bar[kQbAB]);
+          }
+          if (!ok) {
+            umma_commit(&bar[kQbDrain2]);
+            mbar_wait_drain(&bar[kQbDrain2], 0, timeout_ns);
+          }
+        }
+      } else {
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+          if (tc > 0 && !mbar_wait(&bar[kQbAccEmpty], (tc - 1) & 1, ctx, 19)) { ok = false; break; }
+          for (int j = 0; j < nt; ++j, ++g) {
+            if (!mbar_wait(&bar[kQbKFull0 + g % SK], (g / SK) & 1, ctx, 18)) { ok = false; break; }
+            if (!mbar_wait(&bar[kQbEFull0 + (g & 1)], (g >> 1) & 1, ctx, 12)) { ok = false; break; }
+            tc_fence_after();
+            const uint64_t dK = make_sw128_desc(sK0 + (g % SK) * Cfg::kMD, kBoxBytes, 1024);
+            const uint32_t tE = tmem + Cfg::kColX + 128 * (g & 1);
+#pragma unroll
+            for (int k = 0; k < kTile / 16; ++k) {
+              // E for keys 16k..16k+15 sits in key half (k >> 2): 8 columns per step
+              umma_f16_ts(tmem + Cfg::kColA, tE + (k >> 2) * 64 + (k & 3) * 8, desc_advance(dK, k * 2048), id_AB,
+                          (j > 0 || k > 0) ? 1u : 0u);
+            }
+            umma_commit(&bar[kQbKEmpty0 + g % SK]);  // K_j consumed (B_j and A_j)
+            umma_commit(&bar[kQbXFree0 + (g & 1)]);
+            if (kGivenD) umma_commit(&bar[kQbPEmpty0 + g % SP]);  // keeps the slot's arrival count
+          }
+          if (ok) umma_commit(&bar[kQbAB]);  // A (and, from kBWarp, B) of this item complete
+        }
+        if (!ok) {
+          umma_commit(&bar[kQbDrain3]);
+          mbar_wait_drain(&bar[kQbDrain3], 0, timeout_ns);
         }
       }
     }
@@ -573,10 +631,13 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 // 64 KB = 224 KB. TMEM: two dP^T/dS^T buffers [0,256) (lane = key, column =
 // query), dV [256,256+D), dK [256+D,256+2D) (lane = key, column = d).
 //
-// Warp roles (12 warps): 0 TMA for V_j and the P stream; 1 MMA issuer for dP^T
-// (and TMEM owner); 2 TMA for dO_i and Q_i; 3 MMA issuer for dV and dK;
-// 4-11 dS warps (TMEM lane quarter = warp % 4, query half = (warp - 4) / 4),
-// which also write dK_j, dV_j.
+// Warp roles: 0 TMA for V_j and the P stream; 1 MMA issuer for dP^T (and
+// TMEM owner); 2 TMA for dO_i and Q_i; 3 MMA issuer for dV and, at D = 128,
+// dK; 4-11 dS warps (TMEM lane quarter = warp % 4, query half =
+// (warp - 4) / 4), which also write dK_j, dV_j; at D = 64, warp 12 issues dK.
+// At D = 64 each MMA group is short and a thread between two of its groups
+// spends a few hundred cycles on barrier waits and commits even when nothing
+// is outstanding, so three issuing threads keep the pipe fed better.
 template <int D>
 struct DkvCfg {
   static constexpr int kMD = (D / kBoxCols) * kBoxBytes;
@@ -590,7 +651,11 @@ struct DkvCfg {
   static constexpr int kSmemBytes = kTileBytes + kBarBytes + 1024;
   static constexpr int kDSWarps = 8;
   static constexpr int kFirstDSWarp = 4;
-  static constexpr int kThreads = 32 * (kFirstDSWarp + kDSWarps);
+  // D = 64: dV and dK have an issuing thread each (warps 3 and kDKWarp);
+  // D = 128: warp 3 issues both (at D = 128 the split measured slower).
+  static constexpr bool kSplit = D == 64;
+  static constexpr int kDKWarp = kFirstDSWarp + kDSWarps;  // dK issuer (D = 64)
+  static constexpr int kThreads = 32 * (kDKWarp + (kSplit ? 1 : 0));
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kColX = 0;  // + 128 * buffer
   static constexpr uint32_t kColdV = 256;
@@ -610,12 +675,13 @@ enum DkvBar : int {
   kKbXFull0 = 13,   // + TMEM buffer: dP^T_i computed
   kKbEFull0 = 15,   // + TMEM buffer: dS^T_i written (8 dS warps)
   kKbXFree0 = 17,   // + TMEM buffer: dK_i has read dS^T_i
-  kKbAcc = 19,       // dV and dK of an item complete
+  kKbAcc = 19,       // dV and dK of an item complete (a commit from each issuer)
   kKbDrain = 20,
   kKbDrain2 = 21,
   kKbVEmpty = 22,    // the dP^T MMAs of an item are done with V_j
   kKbAccEmpty = 23,  // the dS warps have read an item's dV and dK (8 warps)
-  kNumDkvBars = 24,
+  kKbDrain3 = 24,    // drain of the dK issuer
+  kNumDkvBars = 25,
 };
 static_assert(kNumDkvBars * 8 + 8 <= 256, "dkv barrier area");
 
@@ -655,9 +721,10 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       mbar_init(&bar[kKbEFull0 + s], kEpi);
       mbar_init(&bar[kKbXFree0 + s], 1);
     }
-    mbar_init(&bar[kKbAcc], 1);
+    mbar_init(&bar[kKbAcc], Cfg::kSplit ? 2 : 1);
     mbar_init(&bar[kKbDrain], 1);
     mbar_init(&bar[kKbDrain2], 1);
+    mbar_init(&bar[kKbDrain3], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -795,11 +862,12 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           mbar_wait_drain(&bar[kKbQFull0 + (i & 1)], (i >> 1) & 1, timeout_ns);
       }
     }
-  } else if (warp == 1 || warp == 3) {
-    // ---- Two MMA issuers (one keeps the tensor pipe fed while the other
-    // waits). Warp 1: dP^T_i into TMEM buffer i % 2. Warp 3: dV_j += P^T dO_i
-    // and dK_j += dS^T Q_i in the order dV_0 dK_0 dV_1 dK_1 ...: dK_i goes
-    // first because buffer i % 2 (and so dP^T_{i+2}) waits for it.
+  } else if (warp == 1 || warp == 3 || warp == Cfg::kDKWarp) {
+    // ---- MMA issuers (the others keep the tensor pipe fed while one waits).
+    // Warp 1: dP^T_i into TMEM buffer i % 2. Warp 3: dV_j += P^T dO_i, and
+    // at D = 128 also dK_j += dS^T Q_i in the order dV_0 dK_0 dV_1 dK_1 ...
+    // (dK_i first: it frees buffer i % 2 for dP^T_(i+2)); at D = 64 warp
+    // kDKWarp issues dK.
     if (lane == 0) {
       constexpr bool kB = Elem<T>::kBF16;
       constexpr uint32_t id_dP = make_idesc_f16<kB>(kTile, kTile, false, false);
@@ -833,7 +901,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           umma_commit(&bar[kKbDrain]);
           mbar_wait_drain(&bar[kKbDrain], 0, timeout_ns);
         }
-      } else {
+      } else if (warp == 3 && !Cfg::kSplit) {
         auto issue_dV = [&](int i, int g) -> bool {
           const int s = g & 1;
           const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD), kBoxBytes, 1024);
@@ -884,9 +952,64 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           umma_commit(&bar[kKbDrain2]);
           mbar_wait_drain(&bar[kKbDrain2], 0, timeout_ns);
         }
+      } else if (warp == 3) {
+        int g = 0, tc = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+          // dV of the previous item must have been read out first
+          if (tc > 0 && !mbar_wait(&bar[kKbAccEmpty], (tc - 1) & 1, ctx, 47)) { ok = false; break; }
+          for (int i = 0; i < mt; ++i, ++g) {
+            const int s = g & 1;
+            // dV += P_ij^T dO_i : A = P^T (MN-major, M = key), B = dO_i (MN-major, N = d).
+            if (!mbar_wait(&bar[kKbPFull0 + s], (g >> 1) & 1, ctx, 42)) { ok = false; break; }
+            if (!mbar_wait(&bar[kKbDOFull0 + s], (g >> 1) & 1, ctx, 46)) { ok = false; break; }
+            tc_fence_after();
+            const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD), kBoxBytes, 1024);
+            const uint64_t dP = make_sw128_desc(smem_u32(smem + Cfg::kOffP + s * Cfg::kPT), kBoxBytes, 1024);
+#pragma unroll
+            for (int k = 0; k < kTile / 16; ++k) {
+              umma_f16_ss(tmem + Cfg::kColdV, desc_advance(dP, k * 2048), desc_advance(ddO, k * 2048), id_dV,
+                          (i > 0 || k > 0) ? 1u : 0u);
+            }
+            umma_commit(&bar[kKbDOEmpty0 + s]);
+            umma_commit(&bar[kKbPEmpty0 + s]);
+          }
+          if (ok) umma_commit(&bar[kKbAcc]);
+        }
+        if (!ok) {
+          umma_commit(&bar[kKbDrain2]);
+          mbar_wait_drain(&bar[kKbDrain2], 0, timeout_ns);
+        }
+      } else {
+        int g = 0, tc = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+          // dK of the previous item must have been read out first
+          if (tc > 0 && !mbar_wait(&bar[kKbAccEmpty], (tc - 1) & 1, ctx, 55)) { ok = false; break; }
+          for (int i = 0; i < mt; ++i, ++g) {
+            const int s = g & 1;
+            // dK += dS^T Q_i : A = dS^T from TMEM buffer s (16 queries = 8
+            // packed columns per step), B = Q_i (MN-major, N = d).
+            if (!mbar_wait(&bar[kKbQFull0 + s], (g >> 1) & 1, ctx, 43)) { ok = false; break; }
+            if (!mbar_wait(&bar[kKbEFull0 + s], (g >> 1) & 1, ctx, 44)) { ok = false; break; }
+            tc_fence_after();
+            const uint64_t dQd = make_sw128_desc(smem_u32(smem + Cfg::kOffQ + s * Cfg::kMD), kBoxBytes, 1024);
+            const uint32_t tS = tmem + Cfg::kColX + 128 * s;
+#pragma unroll
+            for (int k = 0; k < kTile / 16; ++k) {
+              umma_f16_ts(tmem + Cfg::kColdK, tS + (k >> 2) * 64 + (k & 3) * 8,
+                          desc_advance(dQd, k * 2048), id_dK, (i > 0 || k > 0) ? 1u : 0u);
+            }
+            umma_commit(&bar[kKbQEmpty0 + s]);
+            umma_commit(&bar[kKbXFree0 + s]);
+          }
+          if (ok) umma_commit(&bar[kKbAcc]);
+        }
+        if (!ok) {
+          umma_commit(&bar[kKbDrain3]);
+          mbar_wait_drain(&bar[kKbDrain3], 0, timeout_ns);
+        }
       }
     }
-  } else if (warp >= Cfg::kFirstDSWarp) {
+  } else if (warp >= Cfg::kFirstDSWarp && warp < Cfg::kFirstDSWarp + Cfg::kDSWarps) {
     // ---- dS warps. Warp w owns TMEM lane quarter qq = w % 4 (keys
     // 32qq..32qq+31 of the tile, as two 16-lane halves) and query half c
     // (queries 64c..64c+63 of each query tile). In the .16x256b fragment,
