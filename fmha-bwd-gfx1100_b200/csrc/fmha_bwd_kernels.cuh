@@ -137,9 +137,9 @@ __device__ __forceinline__ void store_row_32(T* out, const float* v) {
 // D = 64: 3 slots each. A 1 KB exchange area for the two warps that share
 // each TMEM lane quarter (values are handed over through an mbarrier per
 // quarter, so every wait is bounded); barriers.
-// TMEM (512 columns): X0 [0,128), X1 [128,256) hold dP_ij; E_ij is then
-// written over the first 32 columns of each 64-column half; A [256, 256+D),
-// B [256+D, 256+2D).
+// TMEM (512 columns): buffers X_b [128 b, 128 b + 128) hold dP_ij (two at
+// D = 128, three at D = 64); E_ij is then written over the first 32 columns
+// of each 64-column half; A and B (D columns each) follow.
 template <int D>
 struct DqCfg {
   static constexpr int kMD = (D / kBoxCols) * kBoxBytes;  // [128 x D] tile
@@ -165,9 +165,10 @@ struct DqCfg {
   static constexpr int kAWarp = kBWarp + 1;                   // MMA issuer of A (D = 64)
   static constexpr int kThreads = 32 * (kBWarp + 1 + (kSplit ? 1 : 0));
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kColX = 0;  // + 128 * buffer
-  static constexpr uint32_t kColA = 256;
-  static constexpr uint32_t kColB = 256 + D;
+  static constexpr int kNX = D == 128 ? 2 : 3;  // dP/E buffers
+  static constexpr uint32_t kColX = 0;          // + 128 * buffer
+  static constexpr uint32_t kColA = 128 * kNX;
+  static constexpr uint32_t kColB = kColA + D;
   static_assert(kColB + D <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -180,17 +181,17 @@ enum DqBar : int {
   kQbKEmpty0 = 10,  // + slot: commits of B_j and A_j
   kQbPFull0 = 13,   // + slot
   kQbPEmpty0 = 16,  // + slot: MMA commit after B_j + 8 epilogue warps
-  kQbXFull0 = 19,   // + buffer (2)
-  kQbEFull0 = 21,   // + buffer
-  kQbXFree0 = 23,   // + buffer
-  kQbAB = 25,       // A and B of an item complete (a commit from each issuer)
-  kQbDrain = 26,
-  kQbXch0 = 27,     // + lane quarter (4): the two warps of a quarter swap values
-  kQbDrain2 = 31,   // drain of the second MMA issuer
-  kQbDOEmpty = 32,  // the dP MMAs of an item are done with dO_i
-  kQbAccEmpty = 33, // the dS warps have read an item's A and B (8 warps)
-  kQbDrain3 = 34,   // drain of the third MMA issuer
-  kNumDqBars = 35,
+  kQbXFull0 = 19,   // + buffer (up to 3)
+  kQbEFull0 = 22,   // + buffer
+  kQbXFree0 = 25,   // + buffer
+  kQbAB = 28,       // A and B of an item complete (a commit from each issuer)
+  kQbDrain = 29,
+  kQbXch0 = 30,     // + lane quarter (4): the two warps of a quarter swap values
+  kQbDrain2 = 34,   // drain of the second MMA issuer
+  kQbDOEmpty = 35,  // the dP MMAs of an item are done with dO_i
+  kQbAccEmpty = 36, // the dS warps have read an item's A and B (8 warps)
+  kQbDrain3 = 37,   // drain of the third MMA issuer
+  kNumDqBars = 38,
 };
 static_assert(kNumDqBars * 8 + 8 <= 512, "dq barrier area");
 
@@ -205,7 +206,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
               T* __restrict__ dQ, float* __restrict__ Dsum, int M, int N, int H,
               KernelStatus* status, uint64_t timeout_ns) {
   using Cfg = DqCfg<D>;
-  constexpr int SV = Cfg::kSV, SK = Cfg::kSK, SP = Cfg::kSP;
+  constexpr int SV = Cfg::kSV, SK = Cfg::kSK, SP = Cfg::kSP, NX = Cfg::kNX;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -235,7 +236,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       mbar_init(&bar[kQbPFull0 + s], 1);
       mbar_init(&bar[kQbPEmpty0 + s], 1 + Cfg::kEpiWarps);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < Cfg::kNX; ++b) {
       mbar_init(&bar[kQbXFull0 + b], 1);
       mbar_init(&bar[kQbEFull0 + b], Cfg::kEpiWarps);
       mbar_init(&bar[kQbXFree0 + b], 1);
@@ -359,16 +360,16 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
           if (!mbar_wait(&bar[kQbDO], tc & 1, ctx, 13)) { ok = false; break; }
           for (int j = 0; j < nt; ++j, ++g) {
             if (!mbar_wait(&bar[kQbVFull0 + g % SV], (g / SV) & 1, ctx, 10)) { ok = false; break; }
-            if (g >= 2 && !mbar_wait(&bar[kQbXFree0 + (g & 1)], ((g >> 1) - 1) & 1, ctx, 11)) { ok = false; break; }
+            if (g >= NX && !mbar_wait(&bar[kQbXFree0 + g % NX], ((g / NX) - 1) & 1, ctx, 11)) { ok = false; break; }
             tc_fence_after();
             const uint64_t dV = make_sw128_desc(sV0 + (g % SV) * Cfg::kMD, 16, 1024);
-            const uint32_t tX = tmem + Cfg::kColX + 128 * (g & 1);
+            const uint32_t tX = tmem + Cfg::kColX + 128 * (g % NX);
 #pragma unroll
             for (int k = 0; k < D / 16; ++k) {
               const uint32_t off = (k >> 2) * kBoxBytes + (k & 3) * 32;
               umma_f16_ss(tX, desc_advance(ddO, off), desc_advance(dV, off), id_dP, k > 0 ? 1u : 0u);
             }
-            umma_commit(&bar[kQbXFull0 + (g & 1)]);
+            umma_commit(&bar[kQbXFull0 + g % NX]);
             umma_commit(&bar[kQbVEmpty0 + g % SV]);  // V_j consumed
           }
           if (ok) umma_commit(&bar[kQbDOEmpty]);  // dO_i consumed
@@ -394,9 +395,9 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
               }
               umma_commit(&bar[kQbPEmpty0 + g % SP]);  // the tensor core's read of P_ij
             }
-            if (!mbar_wait(&bar[kQbEFull0 + (g & 1)], (g >> 1) & 1, ctx, 12)) { ok = false; break; }
+            if (!mbar_wait(&bar[kQbEFull0 + g % NX], (g / NX) & 1, ctx, 12)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t tE = tmem + Cfg::kColX + 128 * (g & 1);
+            const uint32_t tE = tmem + Cfg::kColX + 128 * (g % NX);
 #pragma unroll
             for (int k = 0; k < kTile / 16; ++k) {
               // E for keys 16k..16k+15 sits in key half (k >> 2): 8 columns per step
@@ -404,7 +405,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
                           (j > 0 || k > 0) ? 1u : 0u);
             }
             umma_commit(&bar[kQbKEmpty0 + g % SK]);  // K_j consumed (B_j and A_j)
-            umma_commit(&bar[kQbXFree0 + (g & 1)]);
+            umma_commit(&bar[kQbXFree0 + g % NX]);
             if (kGivenD) umma_commit(&bar[kQbPEmpty0 + g % SP]);  // keeps the slot's arrival count
           }
           if (ok) umma_commit(&bar[kQbAB]);  // A and B of this item complete
@@ -443,10 +444,10 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
           if (tc > 0 && !mbar_wait(&bar[kQbAccEmpty], (tc - 1) & 1, ctx, 19)) { ok = false; break; }
           for (int j = 0; j < nt; ++j, ++g) {
             if (!mbar_wait(&bar[kQbKFull0 + g % SK], (g / SK) & 1, ctx, 18)) { ok = false; break; }
-            if (!mbar_wait(&bar[kQbEFull0 + (g & 1)], (g >> 1) & 1, ctx, 12)) { ok = false; break; }
+            if (!mbar_wait(&bar[kQbEFull0 + g % NX], (g / NX) & 1, ctx, 12)) { ok = false; break; }
             tc_fence_after();
             const uint64_t dK = make_sw128_desc(sK0 + (g % SK) * Cfg::kMD, kBoxBytes, 1024);
-            const uint32_t tE = tmem + Cfg::kColX + 128 * (g & 1);
+            const uint32_t tE = tmem + Cfg::kColX + 128 * (g % NX);
 #pragma unroll
             for (int k = 0; k < kTile / 16; ++k) {
               // E for keys 16k..16k+15 sits in key half (k >> 2): 8 columns per step
@@ -454,7 +455,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
                           (j > 0 || k > 0) ? 1u : 0u);
             }
             umma_commit(&bar[kQbKEmpty0 + g % SK]);  // K_j consumed (B_j and A_j)
-            umma_commit(&bar[kQbXFree0 + (g & 1)]);
+            umma_commit(&bar[kQbXFree0 + g % NX]);
             if (kGivenD) umma_commit(&bar[kQbPEmpty0 + g % SP]);  // keeps the slot's arrival count
           }
           if (ok) umma_commit(&bar[kQbAB]);  // A (and, from kBWarp, B) of this item complete
@@ -503,8 +504,8 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       if constexpr (kGivenD) shift = m < M ? Dsum[static_cast<int64_t>(h) * M + m] : 0.f;
       for (int j = 0; j < nt; ++j, ++g) {
         const int s = g % SP;
-        const int b = g & 1;
-        if (!mbar_wait(&bar[kQbXFull0 + b], (g >> 1) & 1, ctx, 20)) { ok = false; break; }
+        const int b = g % NX;  // dP/E buffer
+        if (!mbar_wait(&bar[kQbXFull0 + b], (g / NX) & 1, ctx, 20)) { ok = false; break; }
         if (!mbar_wait(&bar[kQbPFull0 + s], (g / SP) & 1, ctx, 21)) { ok = false; break; }
         __syncwarp();
         tc_fence_after();
@@ -657,9 +658,10 @@ struct DkvCfg {
   static constexpr int kDKWarp = kFirstDSWarp + kDSWarps;  // dK issuer (D = 64)
   static constexpr int kThreads = 32 * (kDKWarp + (kSplit ? 1 : 0));
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kColX = 0;  // + 128 * buffer
-  static constexpr uint32_t kColdV = 256;
-  static constexpr uint32_t kColdK = 256 + D;
+  static constexpr int kNX = D == 128 ? 2 : 3;  // dP^T/dS^T buffers
+  static constexpr uint32_t kColX = 0;          // + 128 * buffer
+  static constexpr uint32_t kColdV = 128 * kNX;
+  static constexpr uint32_t kColdK = kColdV + D;
   static_assert(kColdK + D <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -672,16 +674,16 @@ enum DkvBar : int {
   kKbDOEmpty0 = 7,  // + slot: dP^T commit + dV commit
   kKbQFull0 = 9,    // + slot
   kKbQEmpty0 = 11,  // + slot
-  kKbXFull0 = 13,   // + TMEM buffer: dP^T_i computed
-  kKbEFull0 = 15,   // + TMEM buffer: dS^T_i written (8 dS warps)
-  kKbXFree0 = 17,   // + TMEM buffer: dK_i has read dS^T_i
-  kKbAcc = 19,       // dV and dK of an item complete (a commit from each issuer)
-  kKbDrain = 20,
-  kKbDrain2 = 21,
-  kKbVEmpty = 22,    // the dP^T MMAs of an item are done with V_j
-  kKbAccEmpty = 23,  // the dS warps have read an item's dV and dK (8 warps)
-  kKbDrain3 = 24,    // drain of the dK issuer
-  kNumDkvBars = 25,
+  kKbXFull0 = 13,   // + TMEM buffer (up to 3): dP^T_i computed
+  kKbEFull0 = 16,   // + TMEM buffer: dS^T_i written (8 dS warps)
+  kKbXFree0 = 19,   // + TMEM buffer: dK_i has read dS^T_i
+  kKbAcc = 22,       // dV and dK of an item complete (a commit from each issuer)
+  kKbDrain = 23,
+  kKbDrain2 = 24,
+  kKbVEmpty = 25,    // the dP^T MMAs of an item are done with V_j
+  kKbAccEmpty = 26,  // the dS warps have read an item's dV and dK (8 warps)
+  kKbDrain3 = 27,    // drain of the dK issuer
+  kNumDkvBars = 28,
 };
 static_assert(kNumDkvBars * 8 + 8 <= 256, "dkv barrier area");
 
@@ -693,6 +695,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
                int H, KernelStatus* status, uint64_t timeout_ns) {
   using Cfg = DkvCfg<D>;
   constexpr int kEpi = Cfg::kDSWarps;
+  constexpr int NX = Cfg::kNX;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -717,6 +720,8 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       mbar_init(&bar[kKbDOEmpty0 + s], 2);
       mbar_init(&bar[kKbQFull0 + s], 1);
       mbar_init(&bar[kKbQEmpty0 + s], 1);
+    }
+    for (int s = 0; s < Cfg::kNX; ++s) {
       mbar_init(&bar[kKbXFull0 + s], 1);
       mbar_init(&bar[kKbEFull0 + s], kEpi);
       mbar_init(&bar[kKbXFree0 + s], 1);
@@ -884,15 +889,16 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD), 16, 1024);
           if (!mbar_wait(&bar[kKbDOFull0 + s], (g >> 1) & 1, ctx, 40)) { ok = false; break; }
           // buffer g % 2 is free once dK has read dS^T of step g - 2 from it
-          if (g >= 2 && !mbar_wait(&bar[kKbXFree0 + s], ((g >> 1) - 1) & 1, ctx, 41)) { ok = false; break; }
+          const int x = g % NX;
+          if (g >= NX && !mbar_wait(&bar[kKbXFree0 + x], ((g / NX) - 1) & 1, ctx, 41)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
             const uint32_t off = (k >> 2) * kBoxBytes + (k & 3) * 32;
-            umma_f16_ss(tmem + Cfg::kColX + 128 * s, desc_advance(dVt, off), desc_advance(ddO, off), id_dP,
+            umma_f16_ss(tmem + Cfg::kColX + 128 * x, desc_advance(dVt, off), desc_advance(ddO, off), id_dP,
                         k > 0 ? 1u : 0u);
           }
-          umma_commit(&bar[kKbXFull0 + s]);
+          umma_commit(&bar[kKbXFull0 + x]);
           umma_commit(&bar[kKbDOEmpty0 + s]);
         }
         if (ok) umma_commit(&bar[kKbVEmpty]);  // V_j consumed
@@ -925,16 +931,16 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           // dK += dS^T Q_i : A = dS^T from TMEM buffer s (16 queries = 8
           // packed columns per step), B = Q_i (MN-major, N = d).
           if (!mbar_wait(&bar[kKbQFull0 + s], (g >> 1) & 1, ctx, 43)) return false;
-          if (!mbar_wait(&bar[kKbEFull0 + s], (g >> 1) & 1, ctx, 44)) return false;
+          if (!mbar_wait(&bar[kKbEFull0 + g % NX], (g / NX) & 1, ctx, 44)) return false;
           tc_fence_after();
-          const uint32_t tS = tmem + Cfg::kColX + 128 * s;
+          const uint32_t tS = tmem + Cfg::kColX + 128 * (g % NX);
 #pragma unroll
           for (int k = 0; k < kTile / 16; ++k) {
             umma_f16_ts(tmem + Cfg::kColdK, tS + (k >> 2) * 64 + (k & 3) * 8,
                         desc_advance(dQd, k * 2048), id_dK, (i > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&bar[kKbQEmpty0 + s]);
-          umma_commit(&bar[kKbXFree0 + s]);
+          umma_commit(&bar[kKbXFree0 + g % NX]);
           return true;
         };
         int g = 0, tc = 0;
@@ -989,17 +995,17 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
             // dK += dS^T Q_i : A = dS^T from TMEM buffer s (16 queries = 8
             // packed columns per step), B = Q_i (MN-major, N = d).
             if (!mbar_wait(&bar[kKbQFull0 + s], (g >> 1) & 1, ctx, 43)) { ok = false; break; }
-            if (!mbar_wait(&bar[kKbEFull0 + s], (g >> 1) & 1, ctx, 44)) { ok = false; break; }
+            if (!mbar_wait(&bar[kKbEFull0 + g % NX], (g / NX) & 1, ctx, 44)) { ok = false; break; }
             tc_fence_after();
             const uint64_t dQd = make_sw128_desc(smem_u32(smem + Cfg::kOffQ + s * Cfg::kMD), kBoxBytes, 1024);
-            const uint32_t tS = tmem + Cfg::kColX + 128 * s;
+            const uint32_t tS = tmem + Cfg::kColX + 128 * (g % NX);
 #pragma unroll
             for (int k = 0; k < kTile / 16; ++k) {
               umma_f16_ts(tmem + Cfg::kColdK, tS + (k >> 2) * 64 + (k & 3) * 8,
                           desc_advance(dQd, k * 2048), id_dK, (i > 0 || k > 0) ? 1u : 0u);
             }
             umma_commit(&bar[kKbQEmpty0 + s]);
-            umma_commit(&bar[kKbXFree0 + s]);
+            umma_commit(&bar[kKbXFree0 + g % NX]);
           }
           if (ok) umma_commit(&bar[kKbAcc]);
         }
@@ -1037,12 +1043,13 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           Dv[2 * blk + 1] = q + 1 < M ? __ldg(Dsum + drow + q + 1) : 0.f;
         }
       }
-      if (!mbar_wait(&bar[kKbXFull0 + s], (g >> 1) & 1, ctx, 50)) { ok = false; break; }
+      const int x = g % NX;  // TMEM buffer of this step
+      if (!mbar_wait(&bar[kKbXFull0 + x], (g / NX) & 1, ctx, 50)) { ok = false; break; }
       if (!mbar_wait(&bar[kKbPFull0 + s], (g >> 1) & 1, ctx, 51)) { ok = false; break; }
       __syncwarp();
       tc_fence_after();
       const uint32_t sP = smem_u32(smem + Cfg::kOffP + s * Cfg::kPT);
-      const uint32_t tX = tmem + Cfg::kColX + 128 * s + 64 * c;
+      const uint32_t tX = tmem + Cfg::kColX + 128 * x + 64 * c;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const uint32_t lane_addr = static_cast<uint32_t>(32 * qq + 16 * hh) << 16;
@@ -1083,7 +1090,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&bar[kKbEFull0 + s]);
+        mbar_arrive(&bar[kKbEFull0 + x]);
         mbar_arrive(&bar[kKbPEmpty0 + s]);
       }
     }
