@@ -29,29 +29,37 @@ constexpr int kNoAllocMaxDevices = 64;
 struct NoAllocSlot {
   float* dsum = nullptr;
   fmha_sm100::KernelStatus* status = nullptr;
-  int rc = 0;  // cudaError_t of the set-up
+  bool ready = false;
 };
 
 NoAllocSlot g_noalloc_slots[kNoAllocMaxDevices];
-std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
 
 // Once per device, with that device current: device addresses of the two
-// scratch arrays, and the kernels' shared-memory attributes.
-const NoAllocSlot& noalloc_setup(int device) {
-  std::call_once(g_noalloc_once[device], [device] {
-    NoAllocSlot& s = g_noalloc_slots[device];
-    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.dsum), g_noalloc_dsum);
-    if (e == cudaSuccess)
-      e = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.status), g_noalloc_status);
+// scratch arrays, and the kernels' shared-memory attributes. A set-up that
+// fails is not remembered: the next call on that device tries again.
+// Returns cudaSuccess or the error of the failed step.
+cudaError_t noalloc_setup(int device, NoAllocSlot& out) {
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  NoAllocSlot& s = g_noalloc_slots[device];
+  if (!s.ready) {
+    float* dsum = nullptr;
+    fmha_sm100::KernelStatus* status = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&dsum), g_noalloc_dsum);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_noalloc_status);
     if (e == cudaSuccess) {
       fmha_sm100::set_kernel_attrs<bf16>();
       e = cudaGetLastError();
     } else {
       cudaGetLastError();
     }
-    s.rc = static_cast<int>(e);
-  });
-  return g_noalloc_slots[device];
+    if (e != cudaSuccess) return e;
+    s.dsum = dsum;
+    s.status = status;
+    s.ready = true;
+  }
+  out = s;
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -116,10 +124,10 @@ FMHA_API int fmha_bwd_full_noalloc(bf16* dQ, bf16* dK, bf16* dV, const bf16* Q, 
   if (major != 10 || minor != 0)
     return set_error(kErrUnsupportedDevice, "device %d is sm_%d%d; this library needs sm_100", device,
                      major, minor);
-  const NoAllocSlot& slot = noalloc_setup(device);
-  if (slot.rc != 0)
-    return set_error(kErrLaunch, "no-alloc scratch set-up failed: %s",
-                     cudaGetErrorString(static_cast<cudaError_t>(slot.rc)));
+  NoAllocSlot slot;
+  const cudaError_t se = noalloc_setup(device, slot);
+  if (se != cudaSuccess)
+    return set_error(kErrLaunch, "no-alloc scratch set-up failed: %s", cudaGetErrorString(se));
 
   // The status slot must start at zero; D needs no clearing (the dQ kernel
   // writes every row that the dK/dV kernel reads, earlier on the same stream).
@@ -128,11 +136,13 @@ FMHA_API int fmha_bwd_full_noalloc(bf16* dQ, bf16* dK, bf16* dV, const bf16* Q, 
   rc = enqueue_backward<bf16>(dQ, dK, dV, Q, K, V, P, dO, M, N, K_dim, total_heads, slot.dsum,
                               slot.status, stream, nullptr);
   if (rc != kOk) return rc;
+  // read the status word on the caller's stream, then wait for that stream
+  // alone (no device-wide synchronisation)
+  KernelStatus st{};
+  e = cudaMemcpyAsync(&st, slot.status, sizeof(KernelStatus), cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess) return set_error(kErrLaunch, "status read failed: %s", cudaGetErrorString(e));
   e = cudaStreamSynchronize(stream);
   if (e != cudaSuccess) return set_error(kErrLaunch, "kernel failed: %s", cudaGetErrorString(e));
-  KernelStatus st{};
-  e = cudaMemcpy(&st, slot.status, sizeof(KernelStatus), cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return set_error(kErrLaunch, "status read failed: %s", cudaGetErrorString(e));
   if (st.code != 0)
     return set_error(kErrDeviceTimeout, "in-kernel wait gave up (code %d, site %d, block %d)",
                      st.code, st.where, st.block);

@@ -643,12 +643,17 @@ template <int D>
 struct DkvCfg {
   static constexpr int kMD = (D / kBoxCols) * kBoxBytes;
   static constexpr int kPT = 2 * kBoxBytes;
+  // ring depths: D = 128 fills shared memory with two slots each; D = 64
+  // has the room for deeper rings (P 3, dO 4, Q 3)
+  static constexpr int kSP = D == 128 ? 2 : 3;  // P_ij slots
+  static constexpr int kSD = D == 128 ? 2 : 4;  // dO_i slots
+  static constexpr int kSQ = D == 128 ? 2 : 3;  // Q_i slots
   static constexpr int kOffV = 0;
-  static constexpr int kOffP = kOffV + kMD;       // two slots
-  static constexpr int kOffdO = kOffP + 2 * kPT;  // two slots
-  static constexpr int kOffQ = kOffdO + 2 * kMD;  // two slots
-  static constexpr int kTileBytes = kOffQ + 2 * kMD;
-  static constexpr int kBarBytes = 256;
+  static constexpr int kOffP = kOffV + kMD;
+  static constexpr int kOffdO = kOffP + kSP * kPT;
+  static constexpr int kOffQ = kOffdO + kSD * kMD;
+  static constexpr int kTileBytes = kOffQ + kSQ * kMD;
+  static constexpr int kBarBytes = 512;
   static constexpr int kSmemBytes = kTileBytes + kBarBytes + 1024;
   static constexpr int kDSWarps = 8;
   static constexpr int kFirstDSWarp = 4;
@@ -668,24 +673,24 @@ struct DkvCfg {
 
 enum DkvBar : int {
   kKbV = 0,
-  kKbPFull0 = 1,    // + slot (2)
-  kKbPEmpty0 = 3,   // + slot: dV commit + 8 dS warps
-  kKbDOFull0 = 5,   // + slot
-  kKbDOEmpty0 = 7,  // + slot: dP^T commit + dV commit
-  kKbQFull0 = 9,    // + slot
-  kKbQEmpty0 = 11,  // + slot
-  kKbXFull0 = 13,   // + TMEM buffer (up to 3): dP^T_i computed
-  kKbEFull0 = 16,   // + TMEM buffer: dS^T_i written (8 dS warps)
-  kKbXFree0 = 19,   // + TMEM buffer: dK_i has read dS^T_i
-  kKbAcc = 22,       // dV and dK of an item complete (a commit from each issuer)
-  kKbDrain = 23,
-  kKbDrain2 = 24,
-  kKbVEmpty = 25,    // the dP^T MMAs of an item are done with V_j
-  kKbAccEmpty = 26,  // the dS warps have read an item's dV and dK (8 warps)
-  kKbDrain3 = 27,    // drain of the dK issuer
-  kNumDkvBars = 28,
+  kKbPFull0 = 1,    // + slot (up to 3)
+  kKbPEmpty0 = 4,   // + slot: dV commit + 8 dS warps
+  kKbDOFull0 = 7,   // + slot (up to 4)
+  kKbDOEmpty0 = 11, // + slot: dP^T commit + dV commit
+  kKbQFull0 = 15,   // + slot (up to 3)
+  kKbQEmpty0 = 18,  // + slot
+  kKbXFull0 = 21,   // + TMEM buffer (up to 3): dP^T_i computed
+  kKbEFull0 = 24,   // + TMEM buffer: dS^T_i written (8 dS warps)
+  kKbXFree0 = 27,   // + TMEM buffer: dK_i has read dS^T_i
+  kKbAcc = 30,       // dV and dK of an item complete (a commit from each issuer)
+  kKbDrain = 31,
+  kKbDrain2 = 32,
+  kKbVEmpty = 33,    // the dP^T MMAs of an item are done with V_j
+  kKbAccEmpty = 34,  // the dS warps have read an item's dV and dK (8 warps)
+  kKbDrain3 = 35,    // drain of the dK issuer
+  kNumDkvBars = 36,
 };
-static_assert(kNumDkvBars * 8 + 8 <= 256, "dkv barrier area");
+static_assert(kNumDkvBars * 8 + 8 <= 512, "dkv barrier area");
 
 template <typename T, int D>
 __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
@@ -696,6 +701,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
   using Cfg = DkvCfg<D>;
   constexpr int kEpi = Cfg::kDSWarps;
   constexpr int NX = Cfg::kNX;
+  constexpr int SP = Cfg::kSP, SD = Cfg::kSD, SQ = Cfg::kSQ;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -713,11 +719,15 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     mbar_init(&bar[kKbV], 1);
     mbar_init(&bar[kKbVEmpty], 1);
     mbar_init(&bar[kKbAccEmpty], kEpi);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < SP; ++s) {
       mbar_init(&bar[kKbPFull0 + s], 1);
       mbar_init(&bar[kKbPEmpty0 + s], 1 + kEpi);
+    }
+    for (int s = 0; s < SD; ++s) {
       mbar_init(&bar[kKbDOFull0 + s], 1);
       mbar_init(&bar[kKbDOEmpty0 + s], 2);
+    }
+    for (int s = 0; s < SQ; ++s) {
       mbar_init(&bar[kKbQFull0 + s], 1);
       mbar_init(&bar[kKbQEmpty0 + s], 1);
     }
@@ -771,8 +781,8 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           tma_load_3d(smem + Cfg::kOffV + b * kBoxBytes, &tm_V, &bar[kKbV], b * kBoxCols, n0, h, pol_v);
         ++nv;
         for (int i = 0; i < mt; ++i, ++g) {
-          const int s = g & 1;
-          const int u = g >> 1;
+          const int s = g % SP;
+          const int u = g / SP;
           if (i + kAhead < mt) {
             tma_prefetch_l2_3d(&tm_P, n0, (i + kAhead) * kTile, h);
             tma_prefetch_l2_3d(&tm_P, n0 + kBoxCols, (i + kAhead) * kTile, h);
@@ -787,8 +797,8 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       }
       if (*abort_flag) {
         if (nv > 0) mbar_wait_drain(&bar[kKbV], (nv - 1) & 1, timeout_ns);
-        for (int i = (issued > 2 ? issued - 2 : 0); i < issued; ++i)
-          mbar_wait_drain(&bar[kKbPFull0 + (i & 1)], (i >> 1) & 1, timeout_ns);
+        for (int i = (issued > SP ? issued - SP : 0); i < issued; ++i)
+          mbar_wait_drain(&bar[kKbPFull0 + i % SP], (i / SP) & 1, timeout_ns);
       }
     }
   } else if (warp == 2) {
@@ -820,8 +830,8 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       bool failed = false;
       while ((next_do < total || next_q < total) && !failed) {
         bool progressed = false;
-        if (next_do < total && (next_do < 2 || mbar_poll(&bar[kKbDOEmpty0 + (next_do & 1)], ((next_do >> 1) - 1) & 1))) {
-          const int s = next_do & 1;
+        if (next_do < total && (next_do < SD || mbar_poll(&bar[kKbDOEmpty0 + next_do % SD], ((next_do / SD) - 1) & 1))) {
+          const int s = next_do % SD;
           const int hh = head_of(next_do), i = next_do % mt;
           mbar_arrive_expect_tx(&bar[kKbDOFull0 + s], Cfg::kMD);
 #pragma unroll
@@ -835,8 +845,8 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           ++next_do;
           progressed = true;
         }
-        if (next_q < total && (next_q < 2 || mbar_poll(&bar[kKbQEmpty0 + (next_q & 1)], ((next_q >> 1) - 1) & 1))) {
-          const int s = next_q & 1;
+        if (next_q < total && (next_q < SQ || mbar_poll(&bar[kKbQEmpty0 + next_q % SQ], ((next_q / SQ) - 1) & 1))) {
+          const int s = next_q % SQ;
           const int hh = head_of(next_q), i = next_q % mt;
           mbar_arrive_expect_tx(&bar[kKbQFull0 + s], Cfg::kMD);
 #pragma unroll
@@ -861,10 +871,10 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         }
       }
       if (*abort_flag) {
-        for (int i = (next_do > 2 ? next_do - 2 : 0); i < next_do; ++i)
-          mbar_wait_drain(&bar[kKbDOFull0 + (i & 1)], (i >> 1) & 1, timeout_ns);
-        for (int i = (next_q > 2 ? next_q - 2 : 0); i < next_q; ++i)
-          mbar_wait_drain(&bar[kKbQFull0 + (i & 1)], (i >> 1) & 1, timeout_ns);
+        for (int i = (next_do > SD ? next_do - SD : 0); i < next_do; ++i)
+          mbar_wait_drain(&bar[kKbDOFull0 + i % SD], (i / SD) & 1, timeout_ns);
+        for (int i = (next_q > SQ ? next_q - SQ : 0); i < next_q; ++i)
+          mbar_wait_drain(&bar[kKbQFull0 + i % SQ], (i / SQ) & 1, timeout_ns);
       }
     }
   } else if (warp == 1 || warp == 3 || warp == Cfg::kDKWarp) {
@@ -885,9 +895,9 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
         if (!mbar_wait(&bar[kKbV], tc & 1, ctx, 45)) { ok = false; break; }
         for (int i = 0; i < mt; ++i, ++g) {
-          const int s = g & 1;
+          const int s = g % SD;
           const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD), 16, 1024);
-          if (!mbar_wait(&bar[kKbDOFull0 + s], (g >> 1) & 1, ctx, 40)) { ok = false; break; }
+          if (!mbar_wait(&bar[kKbDOFull0 + s], (g / SD) & 1, ctx, 40)) { ok = false; break; }
           // buffer g % 2 is free once dK has read dS^T of step g - 2 from it
           const int x = g % NX;
           if (g >= NX && !mbar_wait(&bar[kKbXFree0 + x], ((g / NX) - 1) & 1, ctx, 41)) { ok = false; break; }
@@ -909,28 +919,28 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         }
       } else if (warp == 3 && !Cfg::kSplit) {
         auto issue_dV = [&](int i, int g) -> bool {
-          const int s = g & 1;
-          const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD), kBoxBytes, 1024);
-          const uint64_t dP = make_sw128_desc(smem_u32(smem + Cfg::kOffP + s * Cfg::kPT), kBoxBytes, 1024);
+          const int sp = g % SP, sd = g % SD;
+          const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + sd * Cfg::kMD), kBoxBytes, 1024);
+          const uint64_t dP = make_sw128_desc(smem_u32(smem + Cfg::kOffP + sp * Cfg::kPT), kBoxBytes, 1024);
           // dV += P_ij^T dO_i : A = P^T (MN-major, M = key), B = dO_i (MN-major, N = d).
-          if (!mbar_wait(&bar[kKbPFull0 + s], (g >> 1) & 1, ctx, 42)) return false;
-          if (!mbar_wait(&bar[kKbDOFull0 + s], (g >> 1) & 1, ctx, 46)) return false;
+          if (!mbar_wait(&bar[kKbPFull0 + sp], (g / SP) & 1, ctx, 42)) return false;
+          if (!mbar_wait(&bar[kKbDOFull0 + sd], (g / SD) & 1, ctx, 46)) return false;
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < kTile / 16; ++k) {
             umma_f16_ss(tmem + Cfg::kColdV, desc_advance(dP, k * 2048), desc_advance(ddO, k * 2048), id_dV,
                         (i > 0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&bar[kKbDOEmpty0 + s]);
-          umma_commit(&bar[kKbPEmpty0 + s]);
+          umma_commit(&bar[kKbDOEmpty0 + sd]);
+          umma_commit(&bar[kKbPEmpty0 + sp]);
           return true;
         };
         auto issue_dK = [&](int i, int g) -> bool {
-          const int s = g & 1;
+          const int s = g % SQ;
           const uint64_t dQd = make_sw128_desc(smem_u32(smem + Cfg::kOffQ + s * Cfg::kMD), kBoxBytes, 1024);
-          // dK += dS^T Q_i : A = dS^T from TMEM buffer s (16 queries = 8
-          // packed columns per step), B = Q_i (MN-major, N = d).
-          if (!mbar_wait(&bar[kKbQFull0 + s], (g >> 1) & 1, ctx, 43)) return false;
+          // dK += dS^T Q_i : A = dS^T from TMEM buffer g % NX (16 queries =
+          // 8 packed columns per step), B = Q_i (MN-major, N = d).
+          if (!mbar_wait(&bar[kKbQFull0 + s], (g / SQ) & 1, ctx, 43)) return false;
           if (!mbar_wait(&bar[kKbEFull0 + g % NX], (g / NX) & 1, ctx, 44)) return false;
           tc_fence_after();
           const uint32_t tS = tmem + Cfg::kColX + 128 * (g % NX);
@@ -964,20 +974,20 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           // dV of the previous item must have been read out first
           if (tc > 0 && !mbar_wait(&bar[kKbAccEmpty], (tc - 1) & 1, ctx, 47)) { ok = false; break; }
           for (int i = 0; i < mt; ++i, ++g) {
-            const int s = g & 1;
+            const int sp = g % SP, sd = g % SD;
             // dV += P_ij^T dO_i : A = P^T (MN-major, M = key), B = dO_i (MN-major, N = d).
-            if (!mbar_wait(&bar[kKbPFull0 + s], (g >> 1) & 1, ctx, 42)) { ok = false; break; }
-            if (!mbar_wait(&bar[kKbDOFull0 + s], (g >> 1) & 1, ctx, 46)) { ok = false; break; }
+            if (!mbar_wait(&bar[kKbPFull0 + sp], (g / SP) & 1, ctx, 42)) { ok = false; break; }
+            if (!mbar_wait(&bar[kKbDOFull0 + sd], (g / SD) & 1, ctx, 46)) { ok = false; break; }
             tc_fence_after();
-            const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD), kBoxBytes, 1024);
-            const uint64_t dP = make_sw128_desc(smem_u32(smem + Cfg::kOffP + s * Cfg::kPT), kBoxBytes, 1024);
+            const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + sd * Cfg::kMD), kBoxBytes, 1024);
+            const uint64_t dP = make_sw128_desc(smem_u32(smem + Cfg::kOffP + sp * Cfg::kPT), kBoxBytes, 1024);
 #pragma unroll
             for (int k = 0; k < kTile / 16; ++k) {
               umma_f16_ss(tmem + Cfg::kColdV, desc_advance(dP, k * 2048), desc_advance(ddO, k * 2048), id_dV,
                           (i > 0 || k > 0) ? 1u : 0u);
             }
-            umma_commit(&bar[kKbDOEmpty0 + s]);
-            umma_commit(&bar[kKbPEmpty0 + s]);
+            umma_commit(&bar[kKbDOEmpty0 + sd]);
+            umma_commit(&bar[kKbPEmpty0 + sp]);
           }
           if (ok) umma_commit(&bar[kKbAcc]);
         }
@@ -991,10 +1001,10 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           // dK of the previous item must have been read out first
           if (tc > 0 && !mbar_wait(&bar[kKbAccEmpty], (tc - 1) & 1, ctx, 55)) { ok = false; break; }
           for (int i = 0; i < mt; ++i, ++g) {
-            const int s = g & 1;
-            // dK += dS^T Q_i : A = dS^T from TMEM buffer s (16 queries = 8
-            // packed columns per step), B = Q_i (MN-major, N = d).
-            if (!mbar_wait(&bar[kKbQFull0 + s], (g >> 1) & 1, ctx, 43)) { ok = false; break; }
+            const int s = g % SQ;
+            // dK += dS^T Q_i : A = dS^T from TMEM buffer g % NX (16 queries =
+            // 8 packed columns per step), B = Q_i (MN-major, N = d).
+            if (!mbar_wait(&bar[kKbQFull0 + s], (g / SQ) & 1, ctx, 43)) { ok = false; break; }
             if (!mbar_wait(&bar[kKbEFull0 + g % NX], (g / NX) & 1, ctx, 44)) { ok = false; break; }
             tc_fence_after();
             const uint64_t dQd = make_sw128_desc(smem_u32(smem + Cfg::kOffQ + s * Cfg::kMD), kBoxBytes, 1024);
@@ -1030,7 +1040,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     const int h = t / ntk;
     const int n0 = (t - h * ntk) * kTile;
     for (int i = 0; i < mt; ++i, ++g) {
-      const int s = g & 1;
+      const int s = g % SP;  // P slot of this step
       // D for this thread's 16 queries (rows of the query tile past M read 0)
       float Dv[16];
       {
@@ -1045,7 +1055,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       }
       const int x = g % NX;  // TMEM buffer of this step
       if (!mbar_wait(&bar[kKbXFull0 + x], (g / NX) & 1, ctx, 50)) { ok = false; break; }
-      if (!mbar_wait(&bar[kKbPFull0 + s], (g >> 1) & 1, ctx, 51)) { ok = false; break; }
+      if (!mbar_wait(&bar[kKbPFull0 + s], (g / SP) & 1, ctx, 51)) { ok = false; break; }
       __syncwarp();
       tc_fence_after();
       const uint32_t sP = smem_u32(smem + Cfg::kOffP + s * Cfg::kPT);

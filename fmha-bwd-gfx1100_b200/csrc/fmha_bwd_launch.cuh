@@ -336,6 +336,8 @@ int run_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const 
   int rc = check_args(dQ, dK, dV, Q, K, V, P, dO, M, N, D, H);
   if (rc != kOk) return rc;
   if (need_given_d && !given_d) return set_error(kErrInvalidArgument, "null D argument");
+  if (given_d && (reinterpret_cast<uintptr_t>(given_d) & 3u) != 0)
+    return set_error(kErrMisaligned, "D must be float-aligned");
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) {
     cudaGetLastError();

@@ -74,20 +74,6 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// As mbar_test, with cluster-scope acquire: for barriers that the other CTA
-// of a pair arrives on (remote arrivals, TMA completions, MMA commits).
-__device__ __forceinline__ bool mbar_test_cl(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
 // Non-blocking probe of a phase (never suspends the thread).
 __device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -142,23 +128,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 0;; ++it) {
     if (mbar_test(bar, parity)) return true;
-    if ((it & 63u) == 63u) {
-      if (*ctx.abort_flag) return false;
-      if (global_timer_ns() - t0 > ctx.timeout_ns || it > (1u << 30)) {
-        note_failure(ctx, where);
-        return false;
-      }
-    }
-  }
-}
-
-// mbar_wait with cluster-scope acquire (see mbar_test_cl).
-__device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity,
-                                             const WaitCtx& ctx, int where) {
-  if (mbar_test_cl(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_test_cl(bar, parity)) return true;
     if ((it & 63u) == 63u) {
       if (*ctx.abort_flag) return false;
       if (global_timer_ns() - t0 > ctx.timeout_ns || it > (1u << 30)) {
@@ -363,106 +332,6 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem,
       : "memory");
 }
 
-// Named barrier over `count` threads (id 1..15; id 0 is __syncthreads).
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
-// --------------------------------------------- CTA pairs (2-SM tcgen05 MMA)
-// A cluster of two CTAs on two SMs runs one M = 256 MMA: each CTA holds its
-// 128 rows of A (and of the accumulator, in its own TMEM) and half of the N
-// rows of B, at the same shared-memory / TMEM offsets; CTA rank 0 (the
-// leader) issues the MMAs. Every tcgen05 instruction of such a kernel uses
-// .cta_group::2.
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// shared::cluster address of the variable at shared::cta address `addr` in
-// CTA `rank` of this cluster.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-
-// All threads of both CTAs (release/acquire at cluster scope). The
-// non-.aligned forms: threads of a warp may arrive at different times.
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release;\n\t"
-               "barrier.cluster.wait.acquire;" ::: "memory");
-}
-
-// Arrive on an mbarrier given by its shared::cluster address (may be in the
-// other CTA of the pair).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-
-// TMA load into this CTA's shared memory whose completion (transaction
-// bytes) is reported on an mbarrier of either CTA of the pair, given by its
-// shared::cluster address. No multicast.
-__device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const void* tmap,
-                                                 uint32_t bar_cluster_addr, int x, int y, int z,
-                                                 uint64_t cache_hint) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster_addr), "r"(x), "r"(y), "r"(z),
-      "l"(cache_hint)
-      : "memory");
-}
-
-// One warp of EACH CTA of the pair (same warp index) executes these.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
-  asm volatile(
-      "tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-          smem_u32(smem_result)),
-      "r"(ncols)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" :: : "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-
-// Pair MMA, A and B from shared memory (issued by the leader only).
-__device__ __forceinline__ void umma2_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Pair MMA, A from TMEM (each CTA's own 128 rows), B from shared memory.
-__device__ __forceinline__ void umma2_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive once on the mbarrier at `cluster_addr` (either CTA of the pair) when
-// every pair MMA issued so far by this thread has completed.
-__device__ __forceinline__ void umma2_commit(uint32_t cluster_addr) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          cluster_addr)
-      : "memory");
-}
-
 // ------------------------------------------------------- UMMA descriptors
 // Shared-memory matrix descriptor (tcgen05 format):
 //   [0,14)  start address >> 4
@@ -524,33 +393,6 @@ __device__ __forceinline__ float2 mul_f32x2(float2 a, float2 b) {
       : "=l"(reinterpret_cast<uint64_t&>(c))
       : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
   return c;
-}
-
-__device__ __forceinline__ float2 fma_f32x2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;"
-      : "=l"(reinterpret_cast<uint64_t&>(d))
-      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)),
-        "l"(reinterpret_cast<const uint64_t&>(c)));
-  return d;
-}
-
-// ------------------------------------------------------------ misc helpers
-__device__ __forceinline__ void red_add_f32(float* gaddr, float v) {
-  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(gaddr), "f"(v) : "memory");
-}
-
-__device__ __forceinline__ void red_add_v4_f32(float* gaddr, float a, float b,
-                                               float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gaddr), "f"(a),
-               "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
-
-__device__ __forceinline__ uint32_t lane_id() {
-  uint32_t l;
-  asm volatile("mov.u32 %0, %%laneid;" : "=r"(l));
-  return l;
 }
 
 }  // namespace fmha_sm100

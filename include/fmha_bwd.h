@@ -88,7 +88,7 @@ int fmha_bwd_full_stream_events(fmha_bf16_t* dQ, fmha_bf16_t* dK,
  * precomputed D" extension the reference's path lacks; no reference
  * counterpart). Dsum[h * M + m] = sum_n P[h,m,n] * dP[h,m,n] in fp32, i.e.
  * rowsum(dO * O) when O = P V is the forward output, supplied by the caller
- * (16-byte aligned device memory, read only). The dQ kernel then skips its
+ * (float-aligned device memory, read only; 2 if misaligned). The dQ kernel then skips its
  * own rowsum and the extra P K accumulation (5 instead of 6 GEMM-sized MMA
  * passes). Stream-ordered; returns 0 or an error code (1 if Dsum is null). */
 int fmha_bwd_full_delta(fmha_bf16_t* dQ, fmha_bf16_t* dK, fmha_bf16_t* dV,
