@@ -580,6 +580,8 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 #pragma unroll
         for (int x = 0; x < kHalf / 32; ++x) {
           uint32_t a[32];
+          __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
+                         // row-guarded stores of the previous iteration
           tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
           if (m < M) store_row_32<T>(out + 32 * x, reinterpret_cast<const float*>(a));
         }
@@ -591,6 +593,8 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 #pragma unroll
         for (int x = 0; x < kHalf / 32; ++x) {
           uint32_t a[32], bb[32];
+          __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
+                         // row-guarded stores of the previous iteration
           tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
           tmem_load_32(lane_base + Cfg::kColB + c * kHalf + 32 * x, bb);
           float v[32];
@@ -1122,6 +1126,8 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
 #pragma unroll
         for (int x = 0; x < kHalf / 32; ++x) {
           uint32_t v[32];
+          __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
+                         // row-guarded stores of the previous iteration
           tmem_load_32(lane_base + col + x * 32, v);
           if (n < N) store_row_32<T>(out + x * 32, reinterpret_cast<const float*>(v));
         }

@@ -360,6 +360,8 @@ __global__ void __launch_bounds__(DqLseCfg<D>::kThreads, 1)
 #pragma unroll
       for (int x = 0; x < kHalf / 32; ++x) {
         uint32_t a[32];
+        __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
+                       // row-guarded stores of the previous iteration
         tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
         float v[32];
 #pragma unroll
@@ -767,6 +769,8 @@ __global__ void __launch_bounds__(DkvLseCfg<D>::kThreads, 1)
 #pragma unroll
         for (int x = 0; x < kHalf / 32; ++x) {
           uint32_t v[32];
+          __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
+                         // row-guarded stores of the previous iteration
           tmem_load_32(lane_base + col + x * 32, v);
           float f[32];
 #pragma unroll

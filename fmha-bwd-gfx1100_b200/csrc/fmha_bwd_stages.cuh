@@ -166,6 +166,8 @@ __global__ void __launch_bounds__(StageGemmCfg::kThreads)
 #pragma unroll
       for (int x = 0; x < kN / 32; ++x) {
         uint32_t v[32];
+        __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
+                       // row-guarded stores of the previous iteration
         tmem_load_32(lane_base + 32 * x, v);
         if (r < R) {
           if (c0 + 32 * x + 32 <= Cc) {
