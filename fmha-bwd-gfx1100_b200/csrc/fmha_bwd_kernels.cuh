@@ -129,6 +129,35 @@ __device__ __forceinline__ void store_row_32(T* out, const float* v) {
   }
 }
 
+// Work units of the persistent kernels. Items are walked by the CTAs in
+// waves of gridDim.x; when the last wave would be less than half full, its
+// items (the tail) are split into `parts` parts each, so they fill one wave:
+// units [0, full) are whole items, units [full, full + parts * tail) are the
+// parts of items full.. (part p covers steps [p len / parts, (p + 1) len /
+// parts) of the item's len steps). A part leaves fp32 partial results in a
+// workspace slot (unit - full); the last part of an item to finish adds them
+// up and writes the item's outputs.
+struct UnitMap {
+  int full;   // whole items
+  int parts;  // parts per tail item (1: no split)
+  int units;  // full + parts * (items - full)
+  __device__ __forceinline__ void get(int u, int len, int& item, int& lo, int& hi, int& part) const {
+    if (u < full) {
+      item = u;
+      lo = 0;
+      hi = len;
+      part = -1;
+      return;
+    }
+    const int v = u - full;
+    const int k = v / parts;
+    item = full + k;
+    part = v - k * parts;
+    lo = (part * len) / parts;
+    hi = ((part + 1) * len) / parts;
+  }
+};
+
 // ================================================================ dq_kernel
 // Shared memory: dO_i [128 x D] resident; three rings, one per streamed
 // operand, so that each slot is released as soon as its own last reader is
@@ -191,7 +220,9 @@ enum DqBar : int {
   kQbDOEmpty = 35,  // the dP MMAs of an item are done with dO_i
   kQbAccEmpty = 36, // the dS warps have read an item's A and B (8 warps)
   kQbDrain3 = 37,   // drain of the third MMA issuer
-  kNumDqBars = 38,
+  kQbPartA = 38,    // the epilogue has written a part's partials (8 warps)
+  kQbPartB = 39,    // whether this part is the item's last is known
+  kNumDqBars = 40,
 };
 static_assert(kNumDqBars * 8 + 8 <= 512, "dq barrier area");
 
@@ -203,8 +234,9 @@ template <typename T, int D, bool kGivenD = false>
 __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
     dq_kernel(const __grid_constant__ CUtensorMap tm_P, const __grid_constant__ CUtensorMap tm_V,
               const __grid_constant__ CUtensorMap tm_K, const __grid_constant__ CUtensorMap tm_dO,
-              T* __restrict__ dQ, float* __restrict__ Dsum, int M, int N, int H,
-              KernelStatus* status, uint64_t timeout_ns) {
+              T* __restrict__ dQ, float* __restrict__ Dsum, int M, int N, int H, UnitMap um,
+              float* __restrict__ part_ws, int* __restrict__ part_cnt, KernelStatus* status,
+              uint64_t timeout_ns) {
   using Cfg = DqCfg<D>;
   constexpr int SV = Cfg::kSV, SK = Cfg::kSK, SP = Cfg::kSP, NX = Cfg::kNX;
   extern __shared__ uint8_t smem_raw[];
@@ -213,13 +245,15 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + kNumDqBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_part = reinterpret_cast<volatile int*>(tmem_slot + 2);
   float* xch = reinterpret_cast<float*>(smem + Cfg::kOffXch);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int mt = (M + kTile - 1) / kTile;
   const int nt = (N + kTile - 1) / kTile;
-  const int tiles = mt * H;  // work items (query tile, head), head-major
+  // work items (query tile, head), head-major, walked as work units (um): a
+  // unit is an item's key tiles [lo, hi)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar[kQbDO], 1);
@@ -247,6 +281,8 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
     mbar_init(&bar[kQbDrain2], 1);
     mbar_init(&bar[kQbDrain3], 1);
     for (int q = 0; q < 4; ++q) mbar_init(&bar[kQbXch0 + q], 2);
+    mbar_init(&bar[kQbPartA], Cfg::kEpiWarps);
+    mbar_init(&bar[kQbPartB], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -260,9 +296,9 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   WaitCtx ctx{abort_flag, timeout_ns};
 
-  // Every role walks the same work items: t = blockIdx.x, + gridDim.x, ...
+  // Every role walks the same work units: u = blockIdx.x, + gridDim.x, ...
   // Shared-memory rings, TMEM buffers and their barrier phases continue
-  // across items (global step counter g over (item, key tile)).
+  // across units (global step counter g over (unit, key tile)).
   if (warp == 0) {
     // ---- TMA producer: per item dO_i (once the previous item's dP MMAs are
     // done), then V_j, P_ij, K_j in the order the tensor core needs them.
@@ -276,22 +312,24 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       constexpr int kAhead = 4;  // P tiles pulled into L2 ahead of the ring
       int g = 0, nV = 0, nP = 0, nK = 0, nD = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x) {
+        int t, lo, hi, part;
+        um.get(u, nt, t, lo, hi, part);
         const int h = t / mt;
         const int m0 = (t - h * mt) * kTile;
         auto prefetch = [&](int j) {
           tma_prefetch_l2_3d(&tm_P, j * kTile, m0, h);
           tma_prefetch_l2_3d(&tm_P, j * kTile + kBoxCols, m0, h);
         };
-        for (int j = 0; j < kAhead && j < nt; ++j) prefetch(j);
+        for (int j = lo; j < lo + kAhead && j < hi; ++j) prefetch(j);
         if (nD > 0 && !mbar_wait(&bar[kQbDOEmpty], (nD - 1) & 1, ctx, 4)) { ok = false; break; }
         mbar_arrive_expect_tx(&bar[kQbDO], Cfg::kMD);
 #pragma unroll
         for (int b = 0; b < D / kBoxCols; ++b)
           tma_load_3d(smem + Cfg::kOffdO + b * kBoxBytes, &tm_dO, &bar[kQbDO], b * kBoxCols, m0, h, pol_kv);
         ++nD;
-        for (int j = 0; j < nt; ++j, ++g) {
-          if (j + kAhead < nt) prefetch(j + kAhead);
+        for (int j = lo; j < hi; ++j, ++g) {
+          if (j + kAhead < hi) prefetch(j + kAhead);
           if (g >= SV && !mbar_wait(&bar[kQbVEmpty0 + g % SV], ((g / SV) - 1) & 1, ctx, 1)) { ok = false; break; }
           {
             uint64_t* fb = &bar[kQbVFull0 + g % SV];
@@ -356,9 +394,11 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       bool ok = true;
       int g = 0, tc = 0;
       if (warp == 1) {
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+        for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
+          int t, lo, hi, part;
+          um.get(u, nt, t, lo, hi, part);
           if (!mbar_wait(&bar[kQbDO], tc & 1, ctx, 13)) { ok = false; break; }
-          for (int j = 0; j < nt; ++j, ++g) {
+          for (int j = lo; j < hi; ++j, ++g) {
             if (!mbar_wait(&bar[kQbVFull0 + g % SV], (g / SV) & 1, ctx, 10)) { ok = false; break; }
             if (g >= NX && !mbar_wait(&bar[kQbXFree0 + g % NX], ((g / NX) - 1) & 1, ctx, 11)) { ok = false; break; }
             tc_fence_after();
@@ -379,9 +419,11 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
           mbar_wait_drain(&bar[kQbDrain], 0, timeout_ns);
         }
       } else if (warp == Cfg::kBWarp && !Cfg::kSplit) {
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+        for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
+          int t, lo, hi, part;
+          um.get(u, nt, t, lo, hi, part);
           if (tc > 0 && !mbar_wait(&bar[kQbAccEmpty], (tc - 1) & 1, ctx, 16)) { ok = false; break; }
-          for (int j = 0; j < nt; ++j, ++g) {
+          for (int j = lo; j < hi; ++j, ++g) {
             if (!kGivenD && !mbar_wait(&bar[kQbPFull0 + g % SP], (g / SP) & 1, ctx, 14)) { ok = false; break; }
             if (!mbar_wait(&bar[kQbKFull0 + g % SK], (g / SK) & 1, ctx, 15)) { ok = false; break; }
             tc_fence_after();
@@ -391,7 +433,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 #pragma unroll
               for (int k = 0; k < kTile / 16; ++k) {
                 umma_f16_ss(tmem + Cfg::kColB, desc_advance(dP, (k >> 2) * kBoxBytes + (k & 3) * 32),
-                            desc_advance(dK, k * 2048), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+                            desc_advance(dK, k * 2048), id_AB, (j > lo || k > 0) ? 1u : 0u);
               }
               umma_commit(&bar[kQbPEmpty0 + g % SP]);  // the tensor core's read of P_ij
             }
@@ -402,7 +444,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
             for (int k = 0; k < kTile / 16; ++k) {
               // E for keys 16k..16k+15 sits in key half (k >> 2): 8 columns per step
               umma_f16_ts(tmem + Cfg::kColA, tE + (k >> 2) * 64 + (k & 3) * 8, desc_advance(dK, k * 2048), id_AB,
-                          (j > 0 || k > 0) ? 1u : 0u);
+                          (j > lo || k > 0) ? 1u : 0u);
             }
             umma_commit(&bar[kQbKEmpty0 + g % SK]);  // K_j consumed (B_j and A_j)
             umma_commit(&bar[kQbXFree0 + g % NX]);
@@ -416,9 +458,11 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
         }
       } else if (warp == Cfg::kBWarp) {
         if constexpr (!kGivenD) {
-          for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+          for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
+            int t, lo, hi, part;
+            um.get(u, nt, t, lo, hi, part);
             if (tc > 0 && !mbar_wait(&bar[kQbAccEmpty], (tc - 1) & 1, ctx, 16)) { ok = false; break; }
-            for (int j = 0; j < nt; ++j, ++g) {
+            for (int j = lo; j < hi; ++j, ++g) {
               if (!mbar_wait(&bar[kQbPFull0 + g % SP], (g / SP) & 1, ctx, 14)) { ok = false; break; }
               if (!mbar_wait(&bar[kQbKFull0 + g % SK], (g / SK) & 1, ctx, 15)) { ok = false; break; }
               tc_fence_after();
@@ -427,7 +471,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 #pragma unroll
               for (int k = 0; k < kTile / 16; ++k) {
                 umma_f16_ss(tmem + Cfg::kColB, desc_advance(dP, (k >> 2) * kBoxBytes + (k & 3) * 32),
-                            desc_advance(dK, k * 2048), id_AB, (j > 0 || k > 0) ? 1u : 0u);
+                            desc_advance(dK, k * 2048), id_AB, (j > lo || k > 0) ? 1u : 0u);
               }
               umma_commit(&bar[kQbPEmpty0 + g % SP]);  // the tensor core's read of P_ij
               umma_commit(&bar[kQbKEmpty0 + g % SK]);
@@ -440,9 +484,11 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
           }
         }
       } else {
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+        for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
+          int t, lo, hi, part;
+          um.get(u, nt, t, lo, hi, part);
           if (tc > 0 && !mbar_wait(&bar[kQbAccEmpty], (tc - 1) & 1, ctx, 19)) { ok = false; break; }
-          for (int j = 0; j < nt; ++j, ++g) {
+          for (int j = lo; j < hi; ++j, ++g) {
             if (!mbar_wait(&bar[kQbKFull0 + g % SK], (g / SK) & 1, ctx, 18)) { ok = false; break; }
             if (!mbar_wait(&bar[kQbEFull0 + g % NX], (g / NX) & 1, ctx, 12)) { ok = false; break; }
             tc_fence_after();
@@ -452,7 +498,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
             for (int k = 0; k < kTile / 16; ++k) {
               // E for keys 16k..16k+15 sits in key half (k >> 2): 8 columns per step
               umma_f16_ts(tmem + Cfg::kColA, tE + (k >> 2) * 64 + (k & 3) * 8, desc_advance(dK, k * 2048), id_AB,
-                          (j > 0 || k > 0) ? 1u : 0u);
+                          (j > lo || k > 0) ? 1u : 0u);
             }
             umma_commit(&bar[kQbKEmpty0 + g % SK]);  // K_j consumed (B_j and A_j)
             umma_commit(&bar[kQbXFree0 + g % NX]);
@@ -495,14 +541,16 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       return xch_round();
     };
     bool ok = true;
-    int g = 0, tc = 0;
-    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+    int g = 0, tc = 0, np = 0;  // np: parts finished (phases of kQbPartA/B)
+    for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
+      int t, lo, hi, part;
+      um.get(u, nt, t, lo, hi, part);
       const int h = t / mt;
       const int m = (t - h * mt) * kTile + r;
-      float Dacc = 0.f;   // this half's sum_n P dP over all key tiles
-      float shift = 0.f;  // c_i (D_i itself when D is given)
+      float Dacc = 0.f;   // this half's sum_n P dP over the unit's key tiles
+      float shift = 0.f;  // c (D_i itself when D is given)
       if constexpr (kGivenD) shift = m < M ? Dsum[static_cast<int64_t>(h) * M + m] : 0.f;
-      for (int j = 0; j < nt; ++j, ++g) {
+      for (int j = lo; j < hi; ++j, ++g) {
         const int s = g % SP;
         const int b = g % NX;  // dP/E buffer
         if (!mbar_wait(&bar[kQbXFull0 + b], (g / NX) & 1, ctx, 20)) { ok = false; break; }
@@ -532,8 +580,9 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
           }
           Dacc += spdp;
         }
-        if (!kGivenD && j == 0) {
-          // shift c_i = P-weighted mean of dP over key tile 0 (both halves)
+        if (!kGivenD && j == lo) {
+          // shift c = P-weighted mean of dP over the unit's first key tile
+          // (both halves)
           float sp = 0.f;
 #pragma unroll
           for (int x = 0; x < 8; ++x) {
@@ -570,43 +619,131 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       }
       if (!ok) break;
       // dQ = A - (D - c) B, and D (or dQ = A when D is given); then hand A
-      // and B back to the issuer
+      // and B back to the issuer. A part of a split item leaves its A, B,
+      // partial D and shift c in the workspace instead; the item's last part
+      // adds them up: dQ = sum_p (A_p - (D - c_p) B_p), D = sum_p D_p.
       if (!mbar_wait(&bar[kQbAB], tc & 1, ctx, 22)) { ok = false; break; }
       __syncwarp();
       tc_fence_after();
       constexpr int kHalf = D / 2;
+      // workspace slot: A [128][D], B [128][D], D_p [128], c_p [128] (fp32)
+      constexpr size_t kSlot = static_cast<size_t>(2) * kTile * D + 2 * kTile;
       T* out = dQ + (static_cast<int64_t>(h) * M + m) * D + c * kHalf;
-      if constexpr (kGivenD) {
-#pragma unroll
-        for (int x = 0; x < kHalf / 32; ++x) {
-          uint32_t a[32];
-          __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
-                         // row-guarded stores of the previous iteration
-          tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
-          if (m < M) store_row_32<T>(out + 32 * x, reinterpret_cast<const float*>(a));
-        }
-      } else {
+      float Dfull = 0.f;
+      if constexpr (!kGivenD) {
         float Dother = 0.f;
         if (!swap(Dacc, Dother)) { ok = false; break; }
-        const float Dfull = Dacc + Dother;
-        const float sD = Dfull - shift;
+        Dfull = Dacc + Dother;
+      }
+      if (part < 0) {
+        if constexpr (kGivenD) {
 #pragma unroll
-        for (int x = 0; x < kHalf / 32; ++x) {
-          uint32_t a[32], bb[32];
-          __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
-                         // row-guarded stores of the previous iteration
-          tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
-          tmem_load_32(lane_base + Cfg::kColB + c * kHalf + 32 * x, bb);
-          float v[32];
+          for (int x = 0; x < kHalf / 32; ++x) {
+            uint32_t a[32];
+            __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
+                           // row-guarded stores of the previous iteration
+            tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
+            if (m < M) store_row_32<T>(out + 32 * x, reinterpret_cast<const float*>(a));
+          }
+        } else {
+          const float sD = Dfull - shift;
 #pragma unroll
-          for (int y = 0; y < 32; ++y) v[y] = fmaf(-sD, __uint_as_float(bb[y]), __uint_as_float(a[y]));
-          if (m < M) store_row_32<T>(out + 32 * x, v);
+          for (int x = 0; x < kHalf / 32; ++x) {
+            uint32_t a[32], bb[32];
+            __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
+                           // row-guarded stores of the previous iteration
+            tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
+            tmem_load_32(lane_base + Cfg::kColB + c * kHalf + 32 * x, bb);
+            float v[32];
+#pragma unroll
+            for (int y = 0; y < 32; ++y) v[y] = fmaf(-sD, __uint_as_float(bb[y]), __uint_as_float(a[y]));
+            if (m < M) store_row_32<T>(out + 32 * x, v);
+          }
+          if (c == 0 && m < M) Dsum[static_cast<int64_t>(h) * M + m] = Dfull;
         }
-        if (c == 0 && m < M) Dsum[static_cast<int64_t>(h) * M + m] = Dfull;
+      } else {
+        float* mine = part_ws + static_cast<size_t>(u - um.full) * kSlot;
+#pragma unroll
+        for (int which = 0; which < (kGivenD ? 1 : 2); ++which) {
+#pragma unroll
+          for (int x = 0; x < kHalf / 32; ++x) {
+            uint32_t a[32];
+            __syncwarp();
+            tmem_load_32(lane_base + (which == 0 ? Cfg::kColA : Cfg::kColB) + c * kHalf + 32 * x, a);
+            float4* dst = reinterpret_cast<float4*>(mine + (static_cast<size_t>(which) * kTile + r) * D +
+                                                    c * kHalf + 32 * x);
+#pragma unroll
+            for (int y = 0; y < 8; ++y)
+              dst[y] = make_float4(__uint_as_float(a[4 * y]), __uint_as_float(a[4 * y + 1]),
+                                   __uint_as_float(a[4 * y + 2]), __uint_as_float(a[4 * y + 3]));
+          }
+        }
+        if (c == 0) {
+          mine[2 * kTile * D + r] = Dfull;
+          mine[2 * kTile * D + kTile + r] = shift;
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kQbAccEmpty]);
+      if (part >= 0) {
+        const int k = (u - um.full) / um.parts;
+        __threadfence();  // this thread's partials, visible device-wide
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[kQbPartA]);
+        if (warp == Cfg::kFirstEpiWarp && lane == 0) {
+          const bool w = mbar_wait(&bar[kQbPartA], np & 1, ctx, 25);
+          if (w) {
+            __threadfence();
+            const int done = atomicAdd(part_cnt + k, 1);
+            const int last = done == um.parts - 1;
+            if (last) part_cnt[k] = 0;  // ready for the next call
+            __threadfence();
+            *last_part = last;
+          }
+          mbar_arrive(&bar[kQbPartB]);
+        }
+        if (!mbar_wait(&bar[kQbPartB], np & 1, ctx, 26)) { ok = false; break; }
+        ++np;
+        if (*abort_flag) { ok = false; break; }
+        if (*last_part) {
+          const float* first = part_ws + static_cast<size_t>(k) * um.parts * kSlot;
+          float Dtot = shift;  // D given: every part carries it as its shift
+          if constexpr (!kGivenD) {
+            Dtot = 0.f;
+            for (int p = 0; p < um.parts; ++p) Dtot += __ldcg(first + p * kSlot + 2 * kTile * D + r);
+          }
+          // 8 columns at a time: sum_p A_p - (D - c_p) B_p (L2 reads,
+          // bypassing L1), rounded to 16-bit, one 16-byte store
+          for (int x = 0; x < kHalf / 8; ++x) {
+            float v[8];
+#pragma unroll
+            for (int y = 0; y < 8; ++y) v[y] = 0.f;
+            for (int p = 0; p < um.parts; ++p) {
+              const float* sp = first + p * kSlot;
+              const float4* pa = reinterpret_cast<const float4*>(sp + static_cast<size_t>(r) * D + c * kHalf + 8 * x);
+              const float4 a0 = __ldcg(pa), a1 = __ldcg(pa + 1);
+              v[0] += a0.x; v[1] += a0.y; v[2] += a0.z; v[3] += a0.w;
+              v[4] += a1.x; v[5] += a1.y; v[6] += a1.z; v[7] += a1.w;
+              if constexpr (!kGivenD) {
+                const float sD = Dtot - __ldcg(sp + 2 * kTile * D + kTile + r);
+                const float4* pb = reinterpret_cast<const float4*>(sp + static_cast<size_t>(kTile + r) * D +
+                                                                   c * kHalf + 8 * x);
+                const float4 b0 = __ldcg(pb), b1 = __ldcg(pb + 1);
+                v[0] = fmaf(-sD, b0.x, v[0]); v[1] = fmaf(-sD, b0.y, v[1]);
+                v[2] = fmaf(-sD, b0.z, v[2]); v[3] = fmaf(-sD, b0.w, v[3]);
+                v[4] = fmaf(-sD, b1.x, v[4]); v[5] = fmaf(-sD, b1.y, v[5]);
+                v[6] = fmaf(-sD, b1.z, v[6]); v[7] = fmaf(-sD, b1.w, v[7]);
+              }
+            }
+            if (m < M)
+              *reinterpret_cast<uint4*>(out + 8 * x) =
+                  make_uint4(Elem<T>::pack(v[0], v[1]), Elem<T>::pack(v[2], v[3]),
+                             Elem<T>::pack(v[4], v[5]), Elem<T>::pack(v[6], v[7]));
+          }
+          if (!kGivenD && c == 0 && m < M) Dsum[static_cast<int64_t>(h) * M + m] = Dtot;
+        }
+      }
     }
   }
 
@@ -692,7 +829,9 @@ enum DkvBar : int {
   kKbVEmpty = 33,    // the dP^T MMAs of an item are done with V_j
   kKbAccEmpty = 34,  // the dS warps have read an item's dV and dK (8 warps)
   kKbDrain3 = 35,    // drain of the dK issuer
-  kNumDkvBars = 36,
+  kKbPartA = 36,     // the dS warps have written a part's partials (8 warps)
+  kKbPartB = 37,     // whether this part is the item's last is known
+  kNumDkvBars = 38,
 };
 static_assert(kNumDkvBars * 8 + 8 <= 512, "dkv barrier area");
 
@@ -701,7 +840,8 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     dkv_kernel(const __grid_constant__ CUtensorMap tm_Q, const __grid_constant__ CUtensorMap tm_V,
                const __grid_constant__ CUtensorMap tm_dO, const __grid_constant__ CUtensorMap tm_P,
                const float* __restrict__ Dsum, T* __restrict__ dK, T* __restrict__ dV, int M, int N,
-               int H, KernelStatus* status, uint64_t timeout_ns) {
+               int H, UnitMap um, float* __restrict__ part_ws, int* __restrict__ part_cnt,
+               KernelStatus* status, uint64_t timeout_ns) {
   using Cfg = DkvCfg<D>;
   constexpr int kEpi = Cfg::kDSWarps;
   constexpr int NX = Cfg::kNX;
@@ -712,12 +852,14 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Cfg::kTileBytes);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + kNumDkvBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_part = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int mt = (M + kTile - 1) / kTile;
   const int ntk = (N + kTile - 1) / kTile;
-  const int tiles = ntk * H;  // work items (key tile, head), head-major
+  // work items (key tile, head), head-major, walked as work units (um): a
+  // unit is an item's query tiles [lo, hi)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar[kKbV], 1);
@@ -744,6 +886,8 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     mbar_init(&bar[kKbDrain], 1);
     mbar_init(&bar[kKbDrain2], 1);
     mbar_init(&bar[kKbDrain3], 1);
+    mbar_init(&bar[kKbPartA], kEpi);
+    mbar_init(&bar[kKbPartB], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -757,9 +901,9 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   WaitCtx ctx{abort_flag, timeout_ns};
 
-  // Every role walks the same work items: t = blockIdx.x, + gridDim.x, ...
+  // Every role walks the same work units: u = blockIdx.x, + gridDim.x, ...
   // Shared-memory rings, TMEM buffers and their barrier phases continue
-  // across items (global step counter g over (item, query tile)).
+  // across units (global step counter g over (unit, query tile)).
   if (warp == 0) {
     // ---- TMA producer: per item V_j (once the previous item's dP^T MMAs are
     // done), then the P stream (2 slots).
@@ -771,10 +915,12 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       constexpr int kAhead = 4;  // P tiles pulled into L2 ahead of the 2-slot ring
       int g = 0, issued = 0, nv = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x) {
+        int t, lo, hi, part;
+        um.get(u, mt, t, lo, hi, part);
         const int h = t / ntk;
         const int n0 = (t - h * ntk) * kTile;
-        for (int i = 0; i < kAhead && i < mt; ++i) {
+        for (int i = lo; i < lo + kAhead && i < hi; ++i) {
           tma_prefetch_l2_3d(&tm_P, n0, i * kTile, h);
           tma_prefetch_l2_3d(&tm_P, n0 + kBoxCols, i * kTile, h);
         }
@@ -784,14 +930,14 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         for (int b = 0; b < D / kBoxCols; ++b)
           tma_load_3d(smem + Cfg::kOffV + b * kBoxBytes, &tm_V, &bar[kKbV], b * kBoxCols, n0, h, pol_v);
         ++nv;
-        for (int i = 0; i < mt; ++i, ++g) {
+        for (int i = lo; i < hi; ++i, ++g) {
           const int s = g % SP;
-          const int u = g / SP;
-          if (i + kAhead < mt) {
+          const int r = g / SP;
+          if (i + kAhead < hi) {
             tma_prefetch_l2_3d(&tm_P, n0, (i + kAhead) * kTile, h);
             tma_prefetch_l2_3d(&tm_P, n0 + kBoxCols, (i + kAhead) * kTile, h);
           }
-          if (u > 0 && !mbar_wait(&bar[kKbPEmpty0 + s], (u - 1) & 1, ctx, 30)) { ok = false; break; }
+          if (r > 0 && !mbar_wait(&bar[kKbPEmpty0 + s], (r - 1) & 1, ctx, 30)) { ok = false; break; }
           uint8_t* dst = smem + Cfg::kOffP + s * Cfg::kPT;
           mbar_arrive_expect_tx(&bar[kKbPFull0 + s], Cfg::kPT);
           tma_load_3d(dst, &tm_P, &bar[kKbPFull0 + s], n0, i * kTile, h, pol_p);
@@ -815,52 +961,69 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       tma_prefetch_desc(&tm_dO);
       tma_prefetch_desc(&tm_Q);
       const uint64_t pol = l2_policy_evict_last();
-      {
-        const int h0 = static_cast<int>(blockIdx.x) / ntk;
-        for (int i = 0; i < kL2Ahead && i < mt; ++i)
-          for (int b = 0; b < D / kBoxCols; ++b) {
-            tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, i * kTile, h0);
-            tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, i * kTile, h0);
-          }
+      // cursors over this CTA's sequence of (unit, query tile): the next dO
+      // load, the next Q load, and the L2 prefetches kL2Ahead tiles ahead
+      struct Cursor {
+        int u, i, hi, h;
+      };
+      auto start = [&](Cursor& c, int u) {
+        c.u = u;
+        if (u < um.units) {
+          int t, lo, hi, part;
+          um.get(u, mt, t, lo, hi, part);
+          c.i = lo;
+          c.hi = hi;
+          c.h = t / ntk;
+        }
+      };
+      auto advance = [&](Cursor& c) {
+        if (++c.i >= c.hi) start(c, c.u + static_cast<int>(gridDim.x));
+      };
+      Cursor cd, cq, pd, pq;
+      start(cd, blockIdx.x);
+      start(cq, blockIdx.x);
+      start(pd, blockIdx.x);
+      start(pq, blockIdx.x);
+      for (int k = 0; k < kL2Ahead && pd.u < um.units; ++k) {
+        for (int b = 0; b < D / kBoxCols; ++b) {
+          tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, pd.i * kTile, pd.h);
+          tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, pq.i * kTile, pq.h);
+        }
+        advance(pd);
+        advance(pq);
       }
-      // global counters over (item, query tile); the query tile of step g is
-      // g % mt and its head is that of item blockIdx.x + (g / mt) * gridDim.x
-      const int my_items = (tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                           static_cast<int>(gridDim.x);
-      const int total = my_items * mt;
-      auto head_of = [&](int g) { return (static_cast<int>(blockIdx.x) + (g / mt) * static_cast<int>(gridDim.x)) / ntk; };
-      int next_do = 0, next_q = 0;
+      int next_do = 0, next_q = 0;  // loads issued (ring phases)
       uint64_t t_last = global_timer_ns();
       bool failed = false;
-      while ((next_do < total || next_q < total) && !failed) {
+      while ((cd.u < um.units || cq.u < um.units) && !failed) {
         bool progressed = false;
-        if (next_do < total && (next_do < SD || mbar_poll(&bar[kKbDOEmpty0 + next_do % SD], ((next_do / SD) - 1) & 1))) {
+        if (cd.u < um.units && (next_do < SD || mbar_poll(&bar[kKbDOEmpty0 + next_do % SD], ((next_do / SD) - 1) & 1))) {
           const int s = next_do % SD;
-          const int hh = head_of(next_do), i = next_do % mt;
           mbar_arrive_expect_tx(&bar[kKbDOFull0 + s], Cfg::kMD);
 #pragma unroll
           for (int b = 0; b < D / kBoxCols; ++b)
             tma_load_3d(smem + Cfg::kOffdO + s * Cfg::kMD + b * kBoxBytes, &tm_dO, &bar[kKbDOFull0 + s],
-                        b * kBoxCols, i * kTile, hh, pol);
-          const int ahead = next_do + kL2Ahead;
-          if (ahead < total)
-            for (int b = 0; b < D / kBoxCols; ++b)
-              tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, (ahead % mt) * kTile, head_of(ahead));
+                        b * kBoxCols, cd.i * kTile, cd.h, pol);
+          if (pd.u < um.units) {
+            for (int b = 0; b < D / kBoxCols; ++b) tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, pd.i * kTile, pd.h);
+            advance(pd);
+          }
+          advance(cd);
           ++next_do;
           progressed = true;
         }
-        if (next_q < total && (next_q < SQ || mbar_poll(&bar[kKbQEmpty0 + next_q % SQ], ((next_q / SQ) - 1) & 1))) {
+        if (cq.u < um.units && (next_q < SQ || mbar_poll(&bar[kKbQEmpty0 + next_q % SQ], ((next_q / SQ) - 1) & 1))) {
           const int s = next_q % SQ;
-          const int hh = head_of(next_q), i = next_q % mt;
           mbar_arrive_expect_tx(&bar[kKbQFull0 + s], Cfg::kMD);
 #pragma unroll
           for (int b = 0; b < D / kBoxCols; ++b)
             tma_load_3d(smem + Cfg::kOffQ + s * Cfg::kMD + b * kBoxBytes, &tm_Q, &bar[kKbQFull0 + s],
-                        b * kBoxCols, i * kTile, hh, pol);
-          const int ahead = next_q + kL2Ahead;
-          if (ahead < total)
-            for (int b = 0; b < D / kBoxCols; ++b)
-              tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, (ahead % mt) * kTile, head_of(ahead));
+                        b * kBoxCols, cq.i * kTile, cq.h, pol);
+          if (pq.u < um.units) {
+            for (int b = 0; b < D / kBoxCols; ++b) tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, pq.i * kTile, pq.h);
+            advance(pq);
+          }
+          advance(cq);
           ++next_q;
           progressed = true;
         }
@@ -896,9 +1059,11 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       bool ok = true;
       if (warp == 1) {
         int g = 0, tc = 0;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+        for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
+        int t, lo, hi, part;
+        um.get(u, mt, t, lo, hi, part);
         if (!mbar_wait(&bar[kKbV], tc & 1, ctx, 45)) { ok = false; break; }
-        for (int i = 0; i < mt; ++i, ++g) {
+        for (int i = lo; i < hi; ++i, ++g) {
           const int s = g % SD;
           const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD), 16, 1024);
           if (!mbar_wait(&bar[kKbDOFull0 + s], (g / SD) & 1, ctx, 40)) { ok = false; break; }
@@ -922,7 +1087,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           mbar_wait_drain(&bar[kKbDrain], 0, timeout_ns);
         }
       } else if (warp == 3 && !Cfg::kSplit) {
-        auto issue_dV = [&](int i, int g) -> bool {
+        auto issue_dV = [&](bool first, int g) -> bool {
           const int sp = g % SP, sd = g % SD;
           const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + sd * Cfg::kMD), kBoxBytes, 1024);
           const uint64_t dP = make_sw128_desc(smem_u32(smem + Cfg::kOffP + sp * Cfg::kPT), kBoxBytes, 1024);
@@ -933,13 +1098,13 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
 #pragma unroll
           for (int k = 0; k < kTile / 16; ++k) {
             umma_f16_ss(tmem + Cfg::kColdV, desc_advance(dP, k * 2048), desc_advance(ddO, k * 2048), id_dV,
-                        (i > 0 || k > 0) ? 1u : 0u);
+                        (!first || k > 0) ? 1u : 0u);
           }
           umma_commit(&bar[kKbDOEmpty0 + sd]);
           umma_commit(&bar[kKbPEmpty0 + sp]);
           return true;
         };
-        auto issue_dK = [&](int i, int g) -> bool {
+        auto issue_dK = [&](bool first, int g) -> bool {
           const int s = g % SQ;
           const uint64_t dQd = make_sw128_desc(smem_u32(smem + Cfg::kOffQ + s * Cfg::kMD), kBoxBytes, 1024);
           // dK += dS^T Q_i : A = dS^T from TMEM buffer g % NX (16 queries =
@@ -951,21 +1116,25 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
 #pragma unroll
           for (int k = 0; k < kTile / 16; ++k) {
             umma_f16_ts(tmem + Cfg::kColdK, tS + (k >> 2) * 64 + (k & 3) * 8,
-                        desc_advance(dQd, k * 2048), id_dK, (i > 0 || k > 0) ? 1u : 0u);
+                        desc_advance(dQd, k * 2048), id_dK, (!first || k > 0) ? 1u : 0u);
           }
           umma_commit(&bar[kKbQEmpty0 + s]);
           umma_commit(&bar[kKbXFree0 + g % NX]);
           return true;
         };
         int g = 0, tc = 0;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc, g += mt) {
-          // dV and dK of the previous item must have been read out first
+        for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
+          int t, lo, hi, part;
+          um.get(u, mt, t, lo, hi, part);
+          const int n = hi - lo;
+          // dV and dK of the previous unit must have been read out first
           if (tc > 0 && !mbar_wait(&bar[kKbAccEmpty], (tc - 1) & 1, ctx, 47)) { ok = false; break; }
-          ok = issue_dV(0, g);
-          for (int i = 0; i < mt && ok; ++i) {
-            if (!issue_dK(i, g + i)) { ok = false; break; }
-            if (i + 1 < mt && !issue_dV(i + 1, g + i + 1)) { ok = false; break; }
+          ok = issue_dV(true, g);
+          for (int i = 0; i < n && ok; ++i) {
+            if (!issue_dK(i == 0, g + i)) { ok = false; break; }
+            if (i + 1 < n && !issue_dV(false, g + i + 1)) { ok = false; break; }
           }
+          g += n;
           if (ok) umma_commit(&bar[kKbAcc]);
         }
         if (!ok) {
@@ -974,10 +1143,12 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         }
       } else if (warp == 3) {
         int g = 0, tc = 0;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
-          // dV of the previous item must have been read out first
+        for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
+          int t, lo, hi, part;
+          um.get(u, mt, t, lo, hi, part);
+          // dV of the previous unit must have been read out first
           if (tc > 0 && !mbar_wait(&bar[kKbAccEmpty], (tc - 1) & 1, ctx, 47)) { ok = false; break; }
-          for (int i = 0; i < mt; ++i, ++g) {
+          for (int i = lo; i < hi; ++i, ++g) {
             const int sp = g % SP, sd = g % SD;
             // dV += P_ij^T dO_i : A = P^T (MN-major, M = key), B = dO_i (MN-major, N = d).
             if (!mbar_wait(&bar[kKbPFull0 + sp], (g / SP) & 1, ctx, 42)) { ok = false; break; }
@@ -988,7 +1159,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
 #pragma unroll
             for (int k = 0; k < kTile / 16; ++k) {
               umma_f16_ss(tmem + Cfg::kColdV, desc_advance(dP, k * 2048), desc_advance(ddO, k * 2048), id_dV,
-                          (i > 0 || k > 0) ? 1u : 0u);
+                          (i > lo || k > 0) ? 1u : 0u);
             }
             umma_commit(&bar[kKbDOEmpty0 + sd]);
             umma_commit(&bar[kKbPEmpty0 + sp]);
@@ -1001,10 +1172,12 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         }
       } else {
         int g = 0, tc = 0;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
-          // dK of the previous item must have been read out first
+        for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
+          int t, lo, hi, part;
+          um.get(u, mt, t, lo, hi, part);
+          // dK of the previous unit must have been read out first
           if (tc > 0 && !mbar_wait(&bar[kKbAccEmpty], (tc - 1) & 1, ctx, 55)) { ok = false; break; }
-          for (int i = 0; i < mt; ++i, ++g) {
+          for (int i = lo; i < hi; ++i, ++g) {
             const int s = g % SQ;
             // dK += dS^T Q_i : A = dS^T from TMEM buffer g % NX (16 queries =
             // 8 packed columns per step), B = Q_i (MN-major, N = d).
@@ -1016,7 +1189,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
 #pragma unroll
             for (int k = 0; k < kTile / 16; ++k) {
               umma_f16_ts(tmem + Cfg::kColdK, tS + (k >> 2) * 64 + (k & 3) * 8,
-                          desc_advance(dQd, k * 2048), id_dK, (i > 0 || k > 0) ? 1u : 0u);
+                          desc_advance(dQd, k * 2048), id_dK, (i > lo || k > 0) ? 1u : 0u);
             }
             umma_commit(&bar[kKbQEmpty0 + s]);
             umma_commit(&bar[kKbXFree0 + g % NX]);
@@ -1039,11 +1212,13 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     const int c = (warp - Cfg::kFirstDSWarp) >> 2;
     const uint32_t lq = static_cast<uint32_t>(lane & 3);
     bool ok = true;
-    int g = 0, tc = 0;
-    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tc) {
+    int g = 0, tc = 0, np = 0;  // np: parts finished (phases of kKbPartA/B)
+    for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
+    int t, lo, hi, part;
+    um.get(u, mt, t, lo, hi, part);
     const int h = t / ntk;
     const int n0 = (t - h * ntk) * kTile;
-    for (int i = 0; i < mt; ++i, ++g) {
+    for (int i = lo; i < hi; ++i, ++g) {
       const int s = g % SP;  // P slot of this step
       // D for this thread's 16 queries (rows of the query tile past M read 0)
       float Dv[16];
@@ -1109,16 +1284,19 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       }
     }
     if (!ok) break;
-    // final dV_j and dK_j rows (lane = key row) -> 16-bit outputs, then hand
-    // the accumulators back to the issuer
+    // final dV_j and dK_j rows (lane = key row) -> 16-bit outputs (a whole
+    // item) or fp32 partials in the workspace (a part of a tail item), then
+    // hand the accumulators back to the issuers
     if (!mbar_wait(&bar[kKbAcc], tc & 1, ctx, 53)) { ok = false; break; }
+    const int r = qq * 32 + lane;
+    const int n = n0 + r;
+    constexpr int kHalf = D / 2;
+    constexpr size_t kSlot = static_cast<size_t>(2) * kTile * D;  // floats per workspace slot
     {
       __syncwarp();
       tc_fence_after();
-      const int r = qq * 32 + lane;
       const uint32_t lane_base = tmem + (static_cast<uint32_t>(qq * 32) << 16);
-      const int n = n0 + r;
-      constexpr int kHalf = D / 2;
+      float* mine = part >= 0 ? part_ws + static_cast<size_t>(u - um.full) * kSlot : nullptr;
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const uint32_t col = (which == 0 ? Cfg::kColdV : Cfg::kColdK) + c * kHalf;
@@ -1129,12 +1307,67 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
                          // row-guarded stores of the previous iteration
           tmem_load_32(lane_base + col + x * 32, v);
-          if (n < N) store_row_32<T>(out + x * 32, reinterpret_cast<const float*>(v));
+          if (part < 0) {
+            if (n < N) store_row_32<T>(out + x * 32, reinterpret_cast<const float*>(v));
+          } else {
+            float4* dst = reinterpret_cast<float4*>(mine + (static_cast<size_t>(which) * kTile + r) * D +
+                                                    c * kHalf + 32 * x);
+#pragma unroll
+            for (int y = 0; y < 8; ++y)
+              dst[y] = make_float4(__uint_as_float(v[4 * y]), __uint_as_float(v[4 * y + 1]),
+                                   __uint_as_float(v[4 * y + 2]), __uint_as_float(v[4 * y + 3]));
+          }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kKbAccEmpty]);
+    }
+    if (part >= 0) {
+      // the last of the item's parts to finish adds the parts' partials up
+      // and writes the item's dV and dK
+      const int k = (u - um.full) / um.parts;
+      __threadfence();  // this thread's partials, visible device-wide
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[kKbPartA]);
+      if (warp == Cfg::kFirstDSWarp && lane == 0) {
+        bool w = mbar_wait(&bar[kKbPartA], np & 1, ctx, 56);
+        if (w) {
+          __threadfence();
+          const int done = atomicAdd(part_cnt + k, 1);
+          const int last = done == um.parts - 1;
+          if (last) part_cnt[k] = 0;  // ready for the next call
+          __threadfence();
+          *last_part = last;
+        }
+        mbar_arrive(&bar[kKbPartB]);
+      }
+      if (!mbar_wait(&bar[kKbPartB], np & 1, ctx, 57)) { ok = false; break; }
+      ++np;
+      if (*abort_flag) { ok = false; break; }
+      if (*last_part) {
+        const float* first = part_ws + static_cast<size_t>(k) * um.parts * kSlot;
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          T* out = (which == 0 ? dV : dK) + (static_cast<int64_t>(h) * N + n) * D + c * kHalf;
+          // 8 columns at a time: sum the parts (L2 reads, bypassing L1),
+          // round to 16-bit, one 16-byte store
+          for (int x = 0; x < kHalf / 8; ++x) {
+            float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+            for (int p = 0; p < um.parts; ++p) {
+              const float4* src = reinterpret_cast<const float4*>(
+                  first + p * kSlot + (static_cast<size_t>(which) * kTile + r) * D + c * kHalf + 8 * x);
+              const float4 f0 = __ldcg(src), f1 = __ldcg(src + 1);
+              a0.x += f0.x; a0.y += f0.y; a0.z += f0.z; a0.w += f0.w;
+              a1.x += f1.x; a1.y += f1.y; a1.z += f1.z; a1.w += f1.w;
+            }
+            if (n < N)
+              *reinterpret_cast<uint4*>(out + 8 * x) =
+                  make_uint4(Elem<T>::pack(a0.x, a0.y), Elem<T>::pack(a0.z, a0.w),
+                             Elem<T>::pack(a1.x, a1.y), Elem<T>::pack(a1.z, a1.w));
+          }
+        }
+      }
     }
     }
   }

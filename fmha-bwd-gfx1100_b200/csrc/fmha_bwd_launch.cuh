@@ -21,6 +21,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <map>
 #include <mutex>
 
@@ -109,6 +110,10 @@ inline bool encode_map(CUtensorMap* map, bool bf16, const void* base, uint64_t c
 struct DeviceWorkspace {
   float* dsum = nullptr;
   size_t dsum_floats = 0;
+  float* part = nullptr;     // fp32 partials of split tail items (dkv_kernel)
+  size_t part_floats = 0;
+  int* part_cnt = nullptr;   // parts finished per split item (reset by the kernel)
+  size_t part_cnt_n = 0;
   KernelStatus* host_status = nullptr;      // mapped pinned host memory
   KernelStatus* host_status_dev = nullptr;  // its device address
   bool attrs_set = false;
@@ -181,10 +186,36 @@ inline bool ensure_status_slot(int device, DeviceWorkspace& w) {
   return true;
 }
 
+// Work units for `items` items of `len` steps each on `grid` CTAs: when the
+// last wave would be at most half full, its items are split into 2..4 parts
+// that fill one wave. Only long items (at least kMinSplitLen steps) are
+// split: a part carries fixed costs (its V tile, a readout of fp32 partials,
+// the combine), and short items are dominated by them and by memory traffic
+// (measured: the 4096 x 512 cross-attention workload, 32-step items, runs
+// slower split; the 16384-row video shards, 128-step items, 9 % faster).
+// Splitting needs a partial-sum workspace; without one (`allow` false) every
+// item stays whole.
+constexpr int kMinSplitLen = 64;
+inline UnitMap plan_units(int items, int grid, int len, bool allow) {
+  UnitMap um{items, 1, items};
+  if (!allow || grid <= 0 || len < kMinSplitLen) return um;
+  const int waves = items / grid, tail = items - waves * grid;
+  if (tail == 0 || 2 * tail > grid) return um;
+  int q = grid / tail;
+  q = q < 4 ? q : 4;
+  q = q < len / 2 ? q : len / 2;
+  if (q < 2) return um;
+  um.full = waves * grid;
+  um.parts = q;
+  um.units = um.full + q * tail;
+  return um;
+}
+
 // Returns the workspace of the current device with at least the requested
 // capacity, or nullptr (error already recorded).
 template <typename T>
-DeviceWorkspace* get_workspace(int device, size_t dsum_floats) {
+DeviceWorkspace* get_workspace(int device, size_t dsum_floats, size_t part_floats = 0,
+                               size_t part_cnt_n = 0) {
   std::lock_guard<std::mutex> g(ws_mutex());
   DeviceWorkspace& w = ws_map()[device];
   if (!ensure_status_slot(device, w)) return nullptr;
@@ -203,6 +234,27 @@ DeviceWorkspace* get_workspace(int device, size_t dsum_floats) {
       return nullptr;
     }
     w.dsum_floats = dsum_floats;
+  }
+  if (part_floats > w.part_floats || part_cnt_n > w.part_cnt_n) {
+    if (w.part) cudaFree(w.part);
+    if (w.part_cnt) cudaFree(w.part_cnt);
+    w.part = nullptr;
+    w.part_cnt = nullptr;
+    w.part_floats = w.part_cnt_n = 0;
+    if (cudaMalloc(&w.part, part_floats * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&w.part_cnt, part_cnt_n * sizeof(int)) != cudaSuccess ||
+        cudaMemset(w.part_cnt, 0, part_cnt_n * sizeof(int)) != cudaSuccess) {
+      cudaGetLastError();
+      if (w.part) cudaFree(w.part);
+      if (w.part_cnt) cudaFree(w.part_cnt);
+      w.part = nullptr;
+      w.part_cnt = nullptr;
+      set_error(kErrOutOfMemory, "workspace allocation of %zu bytes failed",
+                part_floats * sizeof(float));
+      return nullptr;
+    }
+    w.part_floats = part_floats;
+    w.part_cnt_n = part_cnt_n;
   }
   return &w;
 }
@@ -251,7 +303,8 @@ inline int check_args(const void* dQ, const void* dK, const void* dV, const void
 template <typename T>
 int enqueue_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const T* P,
                      const T* dO, int M, int N, int D, int H, float* dsum, KernelStatus* st,
-                     cudaStream_t stream, cudaEvent_t const* events, bool given_d = false) {
+                     cudaStream_t stream, cudaEvent_t const* events, bool given_d = false,
+                     float* part_ws = nullptr, int* part_cnt = nullptr) {
   constexpr bool kBF16 = Elem<T>::kBF16;
   CUtensorMap mQ, mK, mV, mdO, mP;
   if (!encode_fn()) return set_error(kErrNoDriver, "cuTensorMapEncodeTiled is unavailable");
@@ -269,32 +322,39 @@ int enqueue_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, co
   cudaGetDevice(&device);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (sms <= 0) sms = 148;
-  // the dQ kernel is persistent: one CTA per SM walks the (query tile, head) items
-  const long long items = static_cast<long long>(mt) * H;
-  const dim3 grid_rows(static_cast<unsigned>(items < sms ? items : sms));
-  const long long kitems = static_cast<long long>((N + kTile - 1) / kTile) * H;
-  const dim3 grid_cols(static_cast<unsigned>(kitems < sms ? kitems : sms));
+  // both kernels are persistent (one CTA per SM) and walk work units: the
+  // dQ kernel's (query tile, head) items over the key tiles, the dK/dV
+  // kernel's (key tile, head) items over the query tiles; a last wave that
+  // would be at most half full is split into parts (plan_units)
+  const int nt = (N + kTile - 1) / kTile;
+  const bool can_split = part_ws != nullptr && part_cnt != nullptr;
+  const UnitMap umq = plan_units(mt * H, sms, nt, can_split);
+  const dim3 grid_rows(static_cast<unsigned>(umq.units < sms ? umq.units : sms));
+  // the dK/dV kernel walks work units: (key tile, head) items, the last
+  // wave's split into parts when it would be at most half full
+  const UnitMap um = plan_units(nt * H, sms, mt, can_split);
+  const dim3 grid_cols(static_cast<unsigned>(um.units < sms ? um.units : sms));
   mark(0);
   if (D == 128) {
     if (given_d)
       dq_kernel<T, 128, true><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
-          mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
+          mP, mV, mK, mdO, dQ, dsum, M, N, H, umq, part_ws, part_cnt, st, tmo);
     else
       dq_kernel<T, 128><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
-          mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
+          mP, mV, mK, mdO, dQ, dsum, M, N, H, umq, part_ws, part_cnt, st, tmo);
     mark(1);
     dkv_kernel<T, 128><<<grid_cols, DkvCfg<128>::kThreads, DkvCfg<128>::kSmemBytes, stream>>>(
-        mQ, mV, mdO, mP, dsum, dK, dV, M, N, H, st, tmo);
+        mQ, mV, mdO, mP, dsum, dK, dV, M, N, H, um, part_ws, part_cnt, st, tmo);
   } else {
     if (given_d)
       dq_kernel<T, 64, true><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
-          mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
+          mP, mV, mK, mdO, dQ, dsum, M, N, H, umq, part_ws, part_cnt, st, tmo);
     else
       dq_kernel<T, 64><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
-          mP, mV, mK, mdO, dQ, dsum, M, N, H, st, tmo);
+          mP, mV, mK, mdO, dQ, dsum, M, N, H, umq, part_ws, part_cnt, st, tmo);
     mark(1);
     dkv_kernel<T, 64><<<grid_cols, DkvCfg<64>::kThreads, DkvCfg<64>::kSmemBytes, stream>>>(
-        mQ, mV, mdO, mP, dsum, dK, dV, M, N, H, st, tmo);
+        mQ, mV, mdO, mP, dsum, dK, dV, M, N, H, um, part_ws, part_cnt, st, tmo);
   }
   mark(2);
   mark(3);
@@ -350,22 +410,40 @@ int run_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const 
     return set_error(kErrUnsupportedDevice, "device %d is sm_%d%d; this library needs sm_100", device,
                      major, minor);
   const size_t rows = static_cast<size_t>(H) * static_cast<size_t>(M);
-  DeviceWorkspace* w = get_workspace<T>(device, given_d ? 0 : rows);
+  // partial-sum workspace for split tail items (at most one wave of parts),
+  // shared by the two kernels, which run one after the other: dK/dV slots
+  // hold [2][128][K_dim] fp32, dQ slots [2][128][K_dim] + [2][128]
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (sms <= 0) sms = 148;
+  const int mtl = (M + kTile - 1) / kTile, ntl = (N + kTile - 1) / kTile;
+  const UnitMap umk = plan_units(ntl * H, sms, mtl, true);
+  const UnitMap umq = plan_units(mtl * H, sms, ntl, true);
+  const size_t slotk = 2 * static_cast<size_t>(kTile) * D, slotq = slotk + 2 * kTile;
+  const size_t part_floats = std::max(static_cast<size_t>(umk.units - umk.full) * slotk,
+                                      static_cast<size_t>(umq.units - umq.full) * slotq);
+  const size_t part_cnt_n = std::max(static_cast<size_t>(umk.units - umk.full) / umk.parts,
+                                     static_cast<size_t>(umq.units - umq.full) / umq.parts);
+  DeviceWorkspace* w = get_workspace<T>(device, given_d ? 0 : rows, part_floats, part_cnt_n);
   if (!w) return kErrOutOfMemory;
 
   if (sync) memset(w->host_status, 0, sizeof(KernelStatus));
   rc = enqueue_backward<T>(dQ, dK, dV, Q, K, V, P, dO, M, N, D, H,
                            given_d ? const_cast<float*>(given_d) : w->dsum, w->host_status_dev,
-                           stream, events, given_d != nullptr);
+                           stream, events, given_d != nullptr,
+                           part_cnt_n > 0 ? w->part : nullptr, part_cnt_n > 0 ? w->part_cnt : nullptr);
   if (rc != kOk) return rc;
   cudaError_t e = cudaSuccess;
   if (sync) {
     e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess) return set_error(kErrLaunch, "kernel failed: %s", cudaGetErrorString(e));
     const KernelStatus stv = read_status(w->host_status);
-    if (stv.code != 0)
+    if (stv.code != 0) {
+      // an aborted call may leave split-item counters part-way
+      if (w->part_cnt) cudaMemset(w->part_cnt, 0, w->part_cnt_n * sizeof(int));
       return set_error(kErrDeviceTimeout, "in-kernel wait gave up (code %d, site %d, block %d)",
                        stv.code, stv.where, stv.block);
+    }
   }
   return set_error(kOk, "");
 }

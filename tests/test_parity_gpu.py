@@ -300,3 +300,45 @@ def test_extreme_shapes(F, oracle_built, M, N, d, H, name):
         ref = O.oracle_bwd(*(_to_bits(t[sl]) for t in (Q, K, V, P, dO)), name)
         for label, got, r in zip(("dQ", "dK", "dV"), (dQ[sl], dK[sl], dV[sl]), ref[:3]):
             _assert_ok(O, label, _f32(got), r, name)
+
+
+@pytest.mark.parametrize("M,N,d,H,dtype", [(8192, 256, 128, 20, "bf16"), (8192, 384, 64, 13, "fp16"),
+                                          (8200, 128, 128, 37, "bf16"), (256, 8192, 128, 20, "bf16"),
+                                          (200, 8200, 64, 30, "fp16")])
+def test_tail_items_split_into_parts(F, oracle_built, M, N, d, H, dtype):
+    """Long items (64 or more steps) of a last, at most half-full wave are
+    split into 2-4 parts whose fp32 partials the last part to finish adds up:
+    the dK/dV kernel's key-tile items over the query tiles (M >= 8192, 37-40
+    items on 148 SMs), and the dQ kernel's query-tile items over the key tiles
+    (N >= 8192: partial A, B, rowsum and shift per part, dQ = sum_p A_p -
+    (D - c_p) B_p); ragged M and N included. NaN-prefilled outputs must be
+    fully written, repeated calls must agree bit for bit (the part counters
+    reset themselves), and every head must match the fp32 recompute; two
+    heads also the CPU oracle."""
+    O = oracle_built
+    Qb, Kb, Vb, Pb, dOb = O.make_inputs(M, N, d, H, dtype, seed=21)
+    dt = _dt(dtype)
+    ins = [_to_dev(x, dt) for x in (Qb, Kb, Vb, Pb, dOb)]
+    outs = [torch.full_like(ins[0], float("nan")), torch.full_like(ins[1], float("nan")),
+            torch.full_like(ins[2], float("nan"))]
+    a = [t.clone() for t in F.fmha_bwd(*ins, out=outs)]
+    assert not any(torch.isnan(t).any().item() for t in a)
+    b = F.fmha_bwd(*ins)
+    assert torch.equal(a[1], b[1]) and torch.equal(a[2], b[2])
+    rq, rk, rv = _torch_reference(*ins)
+    _assert_ok(O, "dQ", _f32(a[0]), rq.cpu().numpy(), dtype)
+    _assert_ok(O, "dK", _f32(a[1]), rk.cpu().numpy(), dtype)
+    _assert_ok(O, "dV", _f32(a[2]), rv.cpu().numpy(), dtype)
+    assert torch.equal(a[0], b[0])
+    for h in (0, H - 1):
+        sl = slice(h, h + 1)
+        oq, ok_, ov, _ = O.oracle_bwd(Qb[sl], Kb[sl], Vb[sl], Pb[sl], dOb[sl], dtype)
+        _assert_ok(O, "dQ", _f32(a[0][sl]), oq, dtype)
+        _assert_ok(O, "dK", _f32(a[1][sl]), ok_, dtype)
+        _assert_ok(O, "dV", _f32(a[2][sl]), ov, dtype)
+    # the precomputed-rowsum entry through the same split (dQ = sum_p A_p)
+    delta = F.rowsum_delta(ins[3], ins[4], ins[2])
+    c_ = F.fmha_bwd(*ins, delta=delta)
+    torch.cuda.synchronize()
+    for nm, x, y in zip(("dQ", "dK", "dV"), a, c_):
+        _assert_ok(O, nm, _f32(y), _f32(x), dtype)
