@@ -135,8 +135,9 @@ __device__ __forceinline__ void store_row_32(T* out, const float* v) {
 // units [0, full) are whole items, units [full, full + parts * tail) are the
 // parts of items full.. (part p covers steps [p len / parts, (p + 1) len /
 // parts) of the item's len steps). A part leaves fp32 partial results in a
-// workspace slot (unit - full); the last part of an item to finish adds them
-// up and writes the item's outputs.
+// workspace slot (unit - full); a combine kernel, launched after the main
+// kernel on the same stream, adds them up and writes the item's outputs.
+constexpr int kMaxParts = 4;  // parts per split item, at most
 struct UnitMap {
   int full;   // whole items
   int parts;  // parts per tail item (1: no split)
@@ -220,9 +221,7 @@ enum DqBar : int {
   kQbDOEmpty = 35,  // the dP MMAs of an item are done with dO_i
   kQbAccEmpty = 36, // the dS warps have read an item's A and B (8 warps)
   kQbDrain3 = 37,   // drain of the third MMA issuer
-  kQbPartA = 38,    // the epilogue has written a part's partials (8 warps)
-  kQbPartB = 39,    // whether this part is the item's last is known
-  kNumDqBars = 40,
+  kNumDqBars = 38,
 };
 static_assert(kNumDqBars * 8 + 8 <= 512, "dq barrier area");
 
@@ -235,8 +234,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
     dq_kernel(const __grid_constant__ CUtensorMap tm_P, const __grid_constant__ CUtensorMap tm_V,
               const __grid_constant__ CUtensorMap tm_K, const __grid_constant__ CUtensorMap tm_dO,
               T* __restrict__ dQ, float* __restrict__ Dsum, int M, int N, int H, UnitMap um,
-              float* __restrict__ part_ws, int* __restrict__ part_cnt, KernelStatus* status,
-              uint64_t timeout_ns) {
+              float* __restrict__ part_ws, KernelStatus* status, uint64_t timeout_ns) {
   using Cfg = DqCfg<D>;
   constexpr int SV = Cfg::kSV, SK = Cfg::kSK, SP = Cfg::kSP, NX = Cfg::kNX;
   extern __shared__ uint8_t smem_raw[];
@@ -245,7 +243,6 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + kNumDqBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* last_part = reinterpret_cast<volatile int*>(tmem_slot + 2);
   float* xch = reinterpret_cast<float*>(smem + Cfg::kOffXch);
 
   const int warp = threadIdx.x >> 5;
@@ -281,8 +278,6 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
     mbar_init(&bar[kQbDrain2], 1);
     mbar_init(&bar[kQbDrain3], 1);
     for (int q = 0; q < 4; ++q) mbar_init(&bar[kQbXch0 + q], 2);
-    mbar_init(&bar[kQbPartA], Cfg::kEpiWarps);
-    mbar_init(&bar[kQbPartB], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -541,7 +536,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       return xch_round();
     };
     bool ok = true;
-    int g = 0, tc = 0, np = 0;  // np: parts finished (phases of kQbPartA/B)
+    int g = 0, tc = 0;
     for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
       int t, lo, hi, part;
       um.get(u, nt, t, lo, hi, part);
@@ -620,7 +615,7 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       if (!ok) break;
       // dQ = A - (D - c) B, and D (or dQ = A when D is given); then hand A
       // and B back to the issuer. A part of a split item leaves its A, B,
-      // partial D and shift c in the workspace instead; the item's last part
+      // partial D and shift c in the workspace instead, and dq_combine_kernel
       // adds them up: dQ = sum_p (A_p - (D - c_p) B_p), D = sum_p D_p.
       if (!mbar_wait(&bar[kQbAB], tc & 1, ctx, 22)) { ok = false; break; }
       __syncwarp();
@@ -686,64 +681,6 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kQbAccEmpty]);
-      if (part >= 0) {
-        const int k = (u - um.full) / um.parts;
-        __threadfence();  // this thread's partials, visible device-wide
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar[kQbPartA]);
-        if (warp == Cfg::kFirstEpiWarp && lane == 0) {
-          const bool w = mbar_wait(&bar[kQbPartA], np & 1, ctx, 25);
-          if (w) {
-            __threadfence();
-            const int done = atomicAdd(part_cnt + k, 1);
-            const int last = done == um.parts - 1;
-            if (last) part_cnt[k] = 0;  // ready for the next call
-            __threadfence();
-            *last_part = last;
-          }
-          mbar_arrive(&bar[kQbPartB]);
-        }
-        if (!mbar_wait(&bar[kQbPartB], np & 1, ctx, 26)) { ok = false; break; }
-        ++np;
-        if (*abort_flag) { ok = false; break; }
-        if (*last_part) {
-          const float* first = part_ws + static_cast<size_t>(k) * um.parts * kSlot;
-          float Dtot = shift;  // D given: every part carries it as its shift
-          if constexpr (!kGivenD) {
-            Dtot = 0.f;
-            for (int p = 0; p < um.parts; ++p) Dtot += __ldcg(first + p * kSlot + 2 * kTile * D + r);
-          }
-          // 8 columns at a time: sum_p A_p - (D - c_p) B_p (L2 reads,
-          // bypassing L1), rounded to 16-bit, one 16-byte store
-          for (int x = 0; x < kHalf / 8; ++x) {
-            float v[8];
-#pragma unroll
-            for (int y = 0; y < 8; ++y) v[y] = 0.f;
-            for (int p = 0; p < um.parts; ++p) {
-              const float* sp = first + p * kSlot;
-              const float4* pa = reinterpret_cast<const float4*>(sp + static_cast<size_t>(r) * D + c * kHalf + 8 * x);
-              const float4 a0 = __ldcg(pa), a1 = __ldcg(pa + 1);
-              v[0] += a0.x; v[1] += a0.y; v[2] += a0.z; v[3] += a0.w;
-              v[4] += a1.x; v[5] += a1.y; v[6] += a1.z; v[7] += a1.w;
-              if constexpr (!kGivenD) {
-                const float sD = Dtot - __ldcg(sp + 2 * kTile * D + kTile + r);
-                const float4* pb = reinterpret_cast<const float4*>(sp + static_cast<size_t>(kTile + r) * D +
-                                                                   c * kHalf + 8 * x);
-                const float4 b0 = __ldcg(pb), b1 = __ldcg(pb + 1);
-                v[0] = fmaf(-sD, b0.x, v[0]); v[1] = fmaf(-sD, b0.y, v[1]);
-                v[2] = fmaf(-sD, b0.z, v[2]); v[3] = fmaf(-sD, b0.w, v[3]);
-                v[4] = fmaf(-sD, b1.x, v[4]); v[5] = fmaf(-sD, b1.y, v[5]);
-                v[6] = fmaf(-sD, b1.z, v[6]); v[7] = fmaf(-sD, b1.w, v[7]);
-              }
-            }
-            if (m < M)
-              *reinterpret_cast<uint4*>(out + 8 * x) =
-                  make_uint4(Elem<T>::pack(v[0], v[1]), Elem<T>::pack(v[2], v[3]),
-                             Elem<T>::pack(v[4], v[5]), Elem<T>::pack(v[6], v[7]));
-          }
-          if (!kGivenD && c == 0 && m < M) Dsum[static_cast<int64_t>(h) * M + m] = Dtot;
-        }
-      }
     }
   }
 
@@ -829,9 +766,7 @@ enum DkvBar : int {
   kKbVEmpty = 33,    // the dP^T MMAs of an item are done with V_j
   kKbAccEmpty = 34,  // the dS warps have read an item's dV and dK (8 warps)
   kKbDrain3 = 35,    // drain of the dK issuer
-  kKbPartA = 36,     // the dS warps have written a part's partials (8 warps)
-  kKbPartB = 37,     // whether this part is the item's last is known
-  kNumDkvBars = 38,
+  kNumDkvBars = 36,
 };
 static_assert(kNumDkvBars * 8 + 8 <= 512, "dkv barrier area");
 
@@ -840,7 +775,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     dkv_kernel(const __grid_constant__ CUtensorMap tm_Q, const __grid_constant__ CUtensorMap tm_V,
                const __grid_constant__ CUtensorMap tm_dO, const __grid_constant__ CUtensorMap tm_P,
                const float* __restrict__ Dsum, T* __restrict__ dK, T* __restrict__ dV, int M, int N,
-               int H, UnitMap um, float* __restrict__ part_ws, int* __restrict__ part_cnt,
+               int H, UnitMap um, float* __restrict__ part_ws,
                KernelStatus* status, uint64_t timeout_ns) {
   using Cfg = DkvCfg<D>;
   constexpr int kEpi = Cfg::kDSWarps;
@@ -852,7 +787,6 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Cfg::kTileBytes);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + kNumDkvBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* last_part = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -886,8 +820,6 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     mbar_init(&bar[kKbDrain], 1);
     mbar_init(&bar[kKbDrain2], 1);
     mbar_init(&bar[kKbDrain3], 1);
-    mbar_init(&bar[kKbPartA], kEpi);
-    mbar_init(&bar[kKbPartB], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -1212,7 +1144,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     const int c = (warp - Cfg::kFirstDSWarp) >> 2;
     const uint32_t lq = static_cast<uint32_t>(lane & 3);
     bool ok = true;
-    int g = 0, tc = 0, np = 0;  // np: parts finished (phases of kKbPartA/B)
+    int g = 0, tc = 0;
     for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
     int t, lo, hi, part;
     um.get(u, mt, t, lo, hi, part);
@@ -1323,52 +1255,6 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[kKbAccEmpty]);
     }
-    if (part >= 0) {
-      // the last of the item's parts to finish adds the parts' partials up
-      // and writes the item's dV and dK
-      const int k = (u - um.full) / um.parts;
-      __threadfence();  // this thread's partials, visible device-wide
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[kKbPartA]);
-      if (warp == Cfg::kFirstDSWarp && lane == 0) {
-        bool w = mbar_wait(&bar[kKbPartA], np & 1, ctx, 56);
-        if (w) {
-          __threadfence();
-          const int done = atomicAdd(part_cnt + k, 1);
-          const int last = done == um.parts - 1;
-          if (last) part_cnt[k] = 0;  // ready for the next call
-          __threadfence();
-          *last_part = last;
-        }
-        mbar_arrive(&bar[kKbPartB]);
-      }
-      if (!mbar_wait(&bar[kKbPartB], np & 1, ctx, 57)) { ok = false; break; }
-      ++np;
-      if (*abort_flag) { ok = false; break; }
-      if (*last_part) {
-        const float* first = part_ws + static_cast<size_t>(k) * um.parts * kSlot;
-#pragma unroll
-        for (int which = 0; which < 2; ++which) {
-          T* out = (which == 0 ? dV : dK) + (static_cast<int64_t>(h) * N + n) * D + c * kHalf;
-          // 8 columns at a time: sum the parts (L2 reads, bypassing L1),
-          // round to 16-bit, one 16-byte store
-          for (int x = 0; x < kHalf / 8; ++x) {
-            float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
-            for (int p = 0; p < um.parts; ++p) {
-              const float4* src = reinterpret_cast<const float4*>(
-                  first + p * kSlot + (static_cast<size_t>(which) * kTile + r) * D + c * kHalf + 8 * x);
-              const float4 f0 = __ldcg(src), f1 = __ldcg(src + 1);
-              a0.x += f0.x; a0.y += f0.y; a0.z += f0.z; a0.w += f0.w;
-              a1.x += f1.x; a1.y += f1.y; a1.z += f1.z; a1.w += f1.w;
-            }
-            if (n < N)
-              *reinterpret_cast<uint4*>(out + 8 * x) =
-                  make_uint4(Elem<T>::pack(a0.x, a0.y), Elem<T>::pack(a0.z, a0.w),
-                             Elem<T>::pack(a1.x, a1.y), Elem<T>::pack(a1.z, a1.w));
-          }
-        }
-      }
-    }
     }
   }
 
@@ -1379,6 +1265,127 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
+}
+
+// ========================================================== combine kernels
+// The parts of split tail items leave fp32 partials in workspace slots
+// (slot = unit - um.full; the parts of tail item k are slots
+// k * parts .. k * parts + parts - 1). These kernels, stream-ordered after the
+// main kernel, add them up in part order and write the 16-bit outputs: one
+// thread per (tail item, row, 8 columns), reading every part's values before
+// adding any (independent, coalesced L2 reads).
+constexpr int kCombineThreads = 256;
+
+// dq slot: A [128][D], B [128][D], D_p [128], c_p [128].
+// dQ = sum_p A_p - (D - c_p) B_p with D = sum_p D_p, also written to Dsum
+// (D given: dQ = sum_p A_p).
+template <typename T, int D, bool kGivenD>
+__global__ void __launch_bounds__(kCombineThreads)
+    dq_combine_kernel(const float* __restrict__ part_ws, UnitMap um, int M, T* __restrict__ dQ,
+                      float* __restrict__ Dsum) {
+  constexpr int kChunks = D / 8;
+  constexpr size_t kSlot = static_cast<size_t>(2) * kTile * D + 2 * kTile;
+  const int mt = (M + kTile - 1) / kTile;
+  const int tail = (um.units - um.full) / um.parts;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * kCombineThreads + threadIdx.x;
+  const int x = static_cast<int>(idx % kChunks);
+  const int r = static_cast<int>((idx / kChunks) % kTile);
+  const int64_t k = idx / (kChunks * kTile);
+  if (k >= tail) return;
+  const int item = um.full + static_cast<int>(k);
+  const int h = item / mt;
+  const int m = (item - h * mt) * kTile + r;
+  if (m >= M) return;
+  const float* first = part_ws + static_cast<size_t>(k) * um.parts * kSlot;
+  float Dp[kMaxParts], cp[kMaxParts];
+  float4 a[kMaxParts][2], b[kMaxParts][2];
+#pragma unroll
+  for (int p = 0; p < kMaxParts; ++p) {
+    if (p < um.parts) {
+      const float* sp = first + p * kSlot;
+      const float4* pa = reinterpret_cast<const float4*>(sp + static_cast<size_t>(r) * D + 8 * x);
+      a[p][0] = __ldcg(pa);
+      a[p][1] = __ldcg(pa + 1);
+      if constexpr (!kGivenD) {
+        const float4* pb = reinterpret_cast<const float4*>(sp + static_cast<size_t>(kTile + r) * D + 8 * x);
+        b[p][0] = __ldcg(pb);
+        b[p][1] = __ldcg(pb + 1);
+        Dp[p] = __ldcg(sp + 2 * kTile * D + r);
+        cp[p] = __ldcg(sp + 2 * kTile * D + kTile + r);
+      }
+    }
+  }
+  float Dtot = 0.f;
+  if constexpr (!kGivenD) {
+#pragma unroll
+    for (int p = 0; p < kMaxParts; ++p)
+      if (p < um.parts) Dtot += Dp[p];
+  }
+  float v[8];
+#pragma unroll
+  for (int y = 0; y < 8; ++y) v[y] = 0.f;
+#pragma unroll
+  for (int p = 0; p < kMaxParts; ++p) {
+    if (p < um.parts) {
+      v[0] += a[p][0].x; v[1] += a[p][0].y; v[2] += a[p][0].z; v[3] += a[p][0].w;
+      v[4] += a[p][1].x; v[5] += a[p][1].y; v[6] += a[p][1].z; v[7] += a[p][1].w;
+      if constexpr (!kGivenD) {
+        const float sD = Dtot - cp[p];
+        v[0] = fmaf(-sD, b[p][0].x, v[0]); v[1] = fmaf(-sD, b[p][0].y, v[1]);
+        v[2] = fmaf(-sD, b[p][0].z, v[2]); v[3] = fmaf(-sD, b[p][0].w, v[3]);
+        v[4] = fmaf(-sD, b[p][1].x, v[4]); v[5] = fmaf(-sD, b[p][1].y, v[5]);
+        v[6] = fmaf(-sD, b[p][1].z, v[6]); v[7] = fmaf(-sD, b[p][1].w, v[7]);
+      }
+    }
+  }
+  *reinterpret_cast<uint4*>(dQ + (static_cast<int64_t>(h) * M + m) * D + 8 * x) =
+      make_uint4(Elem<T>::pack(v[0], v[1]), Elem<T>::pack(v[2], v[3]), Elem<T>::pack(v[4], v[5]),
+                 Elem<T>::pack(v[6], v[7]));
+  if (!kGivenD && x == 0) Dsum[static_cast<int64_t>(h) * M + m] = Dtot;
+}
+
+// dkv slot: dV [128][D], dK [128][D]; each is the sum of its parts.
+template <typename T, int D>
+__global__ void __launch_bounds__(kCombineThreads)
+    dkv_combine_kernel(const float* __restrict__ part_ws, UnitMap um, int N, T* __restrict__ dK,
+                       T* __restrict__ dV) {
+  constexpr int kChunks = D / 8;
+  constexpr size_t kSlot = static_cast<size_t>(2) * kTile * D;
+  const int ntk = (N + kTile - 1) / kTile;
+  const int tail = (um.units - um.full) / um.parts;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * kCombineThreads + threadIdx.x;
+  const int x = static_cast<int>(idx % kChunks);
+  const int64_t row = idx / kChunks;           // (tail item, which, key row)
+  const int r = static_cast<int>(row % kTile);
+  const int which = static_cast<int>((row / kTile) % 2);
+  const int64_t k = row / (2 * kTile);
+  if (k >= tail) return;
+  const int item = um.full + static_cast<int>(k);
+  const int h = item / ntk;
+  const int n = (item - h * ntk) * kTile + r;
+  if (n >= N) return;
+  const float* src = part_ws + static_cast<size_t>(k) * um.parts * kSlot +
+                     (static_cast<size_t>(which) * kTile + r) * D + 8 * x;
+  float4 f[kMaxParts][2];
+#pragma unroll
+  for (int p = 0; p < kMaxParts; ++p) {
+    if (p < um.parts) {
+      const float4* sp = reinterpret_cast<const float4*>(src + p * kSlot);
+      f[p][0] = __ldcg(sp);
+      f[p][1] = __ldcg(sp + 1);
+    }
+  }
+  float4 a0 = f[0][0], a1 = f[0][1];
+#pragma unroll
+  for (int p = 1; p < kMaxParts; ++p) {
+    if (p < um.parts) {
+      a0.x += f[p][0].x; a0.y += f[p][0].y; a0.z += f[p][0].z; a0.w += f[p][0].w;
+      a1.x += f[p][1].x; a1.y += f[p][1].y; a1.z += f[p][1].z; a1.w += f[p][1].w;
+    }
+  }
+  T* out = (which == 0 ? dV : dK) + (static_cast<int64_t>(h) * N + n) * D + 8 * x;
+  *reinterpret_cast<uint4*>(out) = make_uint4(Elem<T>::pack(a0.x, a0.y), Elem<T>::pack(a0.z, a0.w),
+                                              Elem<T>::pack(a1.x, a1.y), Elem<T>::pack(a1.z, a1.w));
 }
 
 }  // namespace fmha_sm100

@@ -110,10 +110,8 @@ inline bool encode_map(CUtensorMap* map, bool bf16, const void* base, uint64_t c
 struct DeviceWorkspace {
   float* dsum = nullptr;
   size_t dsum_floats = 0;
-  float* part = nullptr;     // fp32 partials of split tail items (dkv_kernel)
+  float* part = nullptr;     // fp32 partials of split tail items
   size_t part_floats = 0;
-  int* part_cnt = nullptr;   // parts finished per split item (reset by the kernel)
-  size_t part_cnt_n = 0;
   KernelStatus* host_status = nullptr;      // mapped pinned host memory
   KernelStatus* host_status_dev = nullptr;  // its device address
   bool attrs_set = false;
@@ -188,14 +186,11 @@ inline bool ensure_status_slot(int device, DeviceWorkspace& w) {
 
 // Work units for `items` items of `len` steps each on `grid` CTAs: when the
 // last wave would be at most half full, its items are split into 2..4 parts
-// that fill one wave. Only long items (at least kMinSplitLen steps) are
-// split: a part carries fixed costs (its V tile, a readout of fp32 partials,
-// the combine), and short items are dominated by them and by memory traffic
-// (measured: the 4096 x 512 cross-attention workload, 32-step items, runs
-// slower split; the 16384-row video shards, 128-step items, 9 % faster).
-// Splitting needs a partial-sum workspace; without one (`allow` false) every
-// item stays whole.
-constexpr int kMinSplitLen = 64;
+// that fill one wave. Items shorter than kMinSplitLen steps stay whole: a
+// part carries fixed costs (its first operand tiles, the readout of fp32
+// partials, a share of the combine kernel). Splitting needs a partial-sum
+// workspace; without one (`allow` false) every item stays whole.
+constexpr int kMinSplitLen = 16;
 inline UnitMap plan_units(int items, int grid, int len, bool allow) {
   UnitMap um{items, 1, items};
   if (!allow || grid <= 0 || len < kMinSplitLen) return um;
@@ -214,8 +209,7 @@ inline UnitMap plan_units(int items, int grid, int len, bool allow) {
 // Returns the workspace of the current device with at least the requested
 // capacity, or nullptr (error already recorded).
 template <typename T>
-DeviceWorkspace* get_workspace(int device, size_t dsum_floats, size_t part_floats = 0,
-                               size_t part_cnt_n = 0) {
+DeviceWorkspace* get_workspace(int device, size_t dsum_floats, size_t part_floats = 0) {
   std::lock_guard<std::mutex> g(ws_mutex());
   DeviceWorkspace& w = ws_map()[device];
   if (!ensure_status_slot(device, w)) return nullptr;
@@ -235,26 +229,18 @@ DeviceWorkspace* get_workspace(int device, size_t dsum_floats, size_t part_float
     }
     w.dsum_floats = dsum_floats;
   }
-  if (part_floats > w.part_floats || part_cnt_n > w.part_cnt_n) {
+  if (part_floats > w.part_floats) {
     if (w.part) cudaFree(w.part);
-    if (w.part_cnt) cudaFree(w.part_cnt);
     w.part = nullptr;
-    w.part_cnt = nullptr;
-    w.part_floats = w.part_cnt_n = 0;
-    if (cudaMalloc(&w.part, part_floats * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&w.part_cnt, part_cnt_n * sizeof(int)) != cudaSuccess ||
-        cudaMemset(w.part_cnt, 0, part_cnt_n * sizeof(int)) != cudaSuccess) {
+    w.part_floats = 0;
+    if (cudaMalloc(&w.part, part_floats * sizeof(float)) != cudaSuccess) {
       cudaGetLastError();
-      if (w.part) cudaFree(w.part);
-      if (w.part_cnt) cudaFree(w.part_cnt);
       w.part = nullptr;
-      w.part_cnt = nullptr;
       set_error(kErrOutOfMemory, "workspace allocation of %zu bytes failed",
                 part_floats * sizeof(float));
       return nullptr;
     }
     w.part_floats = part_floats;
-    w.part_cnt_n = part_cnt_n;
   }
   return &w;
 }
@@ -297,14 +283,17 @@ inline int check_args(const void* dQ, const void* dK, const void* dV, const void
 // Encodes the tensor maps and enqueues the two kernels on `stream`, with D
 // at `dsum` (written by the dQ kernel, or read by both kernels when
 // `given_d` is set) and the wait status at `st`. Arguments are already
-// checked.
+// checked. With a partial-sum workspace (`part_ws`), tail items may be split
+// (plan_units); each kernel with split items is then followed by its combine
+// kernel.
 // Optional timing events: [0] before the dQ kernel, [1] between the two
-// kernels, [2] and [3] after the dK/dV kernel.
+// kernels (after the dQ combine), [2] and [3] after the dK/dV kernel (and
+// its combine).
 template <typename T>
 int enqueue_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const T* P,
                      const T* dO, int M, int N, int D, int H, float* dsum, KernelStatus* st,
                      cudaStream_t stream, cudaEvent_t const* events, bool given_d = false,
-                     float* part_ws = nullptr, int* part_cnt = nullptr) {
+                     float* part_ws = nullptr) {
   constexpr bool kBF16 = Elem<T>::kBF16;
   CUtensorMap mQ, mK, mV, mdO, mP;
   if (!encode_fn()) return set_error(kErrNoDriver, "cuTensorMapEncodeTiled is unavailable");
@@ -327,34 +316,63 @@ int enqueue_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, co
   // kernel's (key tile, head) items over the query tiles; a last wave that
   // would be at most half full is split into parts (plan_units)
   const int nt = (N + kTile - 1) / kTile;
-  const bool can_split = part_ws != nullptr && part_cnt != nullptr;
+  const bool can_split = part_ws != nullptr;
   const UnitMap umq = plan_units(mt * H, sms, nt, can_split);
   const dim3 grid_rows(static_cast<unsigned>(umq.units < sms ? umq.units : sms));
   // the dK/dV kernel walks work units: (key tile, head) items, the last
   // wave's split into parts when it would be at most half full
   const UnitMap um = plan_units(nt * H, sms, mt, can_split);
   const dim3 grid_cols(static_cast<unsigned>(um.units < sms ? um.units : sms));
+  // combine grids: one thread per (tail item, row, 8 columns); dK/dV rows
+  // count twice (dV and dK)
+  auto combine_blocks = [&](const UnitMap& u, int rows_per_item) {
+    const int64_t tail = (u.units - u.full) / u.parts;
+    const int64_t threads = tail * rows_per_item * kTile * (D / 8);
+    return dim3(static_cast<unsigned>((threads + kCombineThreads - 1) / kCombineThreads));
+  };
   mark(0);
   if (D == 128) {
     if (given_d)
       dq_kernel<T, 128, true><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
-          mP, mV, mK, mdO, dQ, dsum, M, N, H, umq, part_ws, part_cnt, st, tmo);
+          mP, mV, mK, mdO, dQ, dsum, M, N, H, umq, part_ws, st, tmo);
     else
       dq_kernel<T, 128><<<grid_rows, DqCfg<128>::kThreads, DqCfg<128>::kSmemBytes, stream>>>(
-          mP, mV, mK, mdO, dQ, dsum, M, N, H, umq, part_ws, part_cnt, st, tmo);
+          mP, mV, mK, mdO, dQ, dsum, M, N, H, umq, part_ws, st, tmo);
+    if (umq.parts > 1) {
+      if (given_d)
+        dq_combine_kernel<T, 128, true><<<combine_blocks(umq, 1), kCombineThreads, 0, stream>>>(
+            part_ws, umq, M, dQ, dsum);
+      else
+        dq_combine_kernel<T, 128, false><<<combine_blocks(umq, 1), kCombineThreads, 0, stream>>>(
+            part_ws, umq, M, dQ, dsum);
+    }
     mark(1);
     dkv_kernel<T, 128><<<grid_cols, DkvCfg<128>::kThreads, DkvCfg<128>::kSmemBytes, stream>>>(
-        mQ, mV, mdO, mP, dsum, dK, dV, M, N, H, um, part_ws, part_cnt, st, tmo);
+        mQ, mV, mdO, mP, dsum, dK, dV, M, N, H, um, part_ws, st, tmo);
+    if (um.parts > 1)
+      dkv_combine_kernel<T, 128><<<combine_blocks(um, 2), kCombineThreads, 0, stream>>>(part_ws, um, N,
+                                                                                          dK, dV);
   } else {
     if (given_d)
       dq_kernel<T, 64, true><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
-          mP, mV, mK, mdO, dQ, dsum, M, N, H, umq, part_ws, part_cnt, st, tmo);
+          mP, mV, mK, mdO, dQ, dsum, M, N, H, umq, part_ws, st, tmo);
     else
       dq_kernel<T, 64><<<grid_rows, DqCfg<64>::kThreads, DqCfg<64>::kSmemBytes, stream>>>(
-          mP, mV, mK, mdO, dQ, dsum, M, N, H, umq, part_ws, part_cnt, st, tmo);
+          mP, mV, mK, mdO, dQ, dsum, M, N, H, umq, part_ws, st, tmo);
+    if (umq.parts > 1) {
+      if (given_d)
+        dq_combine_kernel<T, 64, true><<<combine_blocks(umq, 1), kCombineThreads, 0, stream>>>(
+            part_ws, umq, M, dQ, dsum);
+      else
+        dq_combine_kernel<T, 64, false><<<combine_blocks(umq, 1), kCombineThreads, 0, stream>>>(
+            part_ws, umq, M, dQ, dsum);
+    }
     mark(1);
     dkv_kernel<T, 64><<<grid_cols, DkvCfg<64>::kThreads, DkvCfg<64>::kSmemBytes, stream>>>(
-        mQ, mV, mdO, mP, dsum, dK, dV, M, N, H, um, part_ws, part_cnt, st, tmo);
+        mQ, mV, mdO, mP, dsum, dK, dV, M, N, H, um, part_ws, st, tmo);
+    if (um.parts > 1)
+      dkv_combine_kernel<T, 64><<<combine_blocks(um, 2), kCombineThreads, 0, stream>>>(part_ws, um, N,
+                                                                                         dK, dV);
   }
   mark(2);
   mark(3);
@@ -422,16 +440,13 @@ int run_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const 
   const size_t slotk = 2 * static_cast<size_t>(kTile) * D, slotq = slotk + 2 * kTile;
   const size_t part_floats = std::max(static_cast<size_t>(umk.units - umk.full) * slotk,
                                       static_cast<size_t>(umq.units - umq.full) * slotq);
-  const size_t part_cnt_n = std::max(static_cast<size_t>(umk.units - umk.full) / umk.parts,
-                                     static_cast<size_t>(umq.units - umq.full) / umq.parts);
-  DeviceWorkspace* w = get_workspace<T>(device, given_d ? 0 : rows, part_floats, part_cnt_n);
+  DeviceWorkspace* w = get_workspace<T>(device, given_d ? 0 : rows, part_floats);
   if (!w) return kErrOutOfMemory;
 
   if (sync) memset(w->host_status, 0, sizeof(KernelStatus));
   rc = enqueue_backward<T>(dQ, dK, dV, Q, K, V, P, dO, M, N, D, H,
                            given_d ? const_cast<float*>(given_d) : w->dsum, w->host_status_dev,
-                           stream, events, given_d != nullptr,
-                           part_cnt_n > 0 ? w->part : nullptr, part_cnt_n > 0 ? w->part_cnt : nullptr);
+                           stream, events, given_d != nullptr, part_floats > 0 ? w->part : nullptr);
   if (rc != kOk) return rc;
   cudaError_t e = cudaSuccess;
   if (sync) {
@@ -439,8 +454,6 @@ int run_backward(T* dQ, T* dK, T* dV, const T* Q, const T* K, const T* V, const 
     if (e != cudaSuccess) return set_error(kErrLaunch, "kernel failed: %s", cudaGetErrorString(e));
     const KernelStatus stv = read_status(w->host_status);
     if (stv.code != 0) {
-      // an aborted call may leave split-item counters part-way
-      if (w->part_cnt) cudaMemset(w->part_cnt, 0, w->part_cnt_n * sizeof(int));
       return set_error(kErrDeviceTimeout, "in-kernel wait gave up (code %d, site %d, block %d)",
                        stv.code, stv.where, stv.block);
     }
