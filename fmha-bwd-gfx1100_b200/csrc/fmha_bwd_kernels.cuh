@@ -129,6 +129,41 @@ __device__ __forceinline__ void store_row_32(T* out, const float* v) {
   }
 }
 
+// Coalesced store of 16-bit output rows held one row per lane: lane l has
+// the S 16-byte chunks (8 values each) of row l, at byte offset 16 j of the
+// row for chunk j. An S x S transpose of the chunks within each group of S
+// lanes (log2 S butterfly stages of __shfl_xor_sync; stage m swaps bit m of
+// the lane and chunk indices) leaves lane l with chunk l % S of rows
+// S (l / S) + k, k = 0..S-1, so that each of the S stores writes 32 / S
+// whole 16 S-byte row segments instead of 32 scattered 16-byte pieces.
+// Rows at or past `valid` are not written. All 32 lanes must call this.
+template <int S>
+__device__ __forceinline__ void store_rows_coalesced(uint4 (&c)[S], uint8_t* row0, size_t pitch,
+                                                     int lane, int valid) {
+#pragma unroll
+  for (int m = 1; m < S; m <<= 1) {
+    const bool hi = (lane & m) != 0;
+#pragma unroll
+    for (int j = 0; j < S; ++j) {
+      if (j & m) continue;
+      const uint4 snd = hi ? c[j] : c[j ^ m];
+      uint4 rcv;
+      rcv.x = __shfl_xor_sync(0xffffffffu, snd.x, m);
+      rcv.y = __shfl_xor_sync(0xffffffffu, snd.y, m);
+      rcv.z = __shfl_xor_sync(0xffffffffu, snd.z, m);
+      rcv.w = __shfl_xor_sync(0xffffffffu, snd.w, m);
+      if (hi) c[j] = rcv;
+      else c[j ^ m] = rcv;
+    }
+  }
+  const int g0 = lane & ~(S - 1), i = lane & (S - 1);
+#pragma unroll
+  for (int k = 0; k < S; ++k) {
+    const int row = g0 + k;
+    if (row < valid) *reinterpret_cast<uint4*>(row0 + static_cast<size_t>(row) * pitch + 16 * i) = c[k];
+  }
+}
+
 // Work units of the persistent kernels. Items are walked by the CTAs in
 // waves of gridDim.x; when the last wave would be less than half full, its
 // items (the tail) are split into `parts` parts each, so they fill one wave:
@@ -623,7 +658,6 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       constexpr int kHalf = D / 2;
       // workspace slot: A [128][D], B [128][D], D_p [128], c_p [128] (fp32)
       constexpr size_t kSlot = static_cast<size_t>(2) * kTile * D + 2 * kTile;
-      T* out = dQ + (static_cast<int64_t>(h) * M + m) * D + c * kHalf;
       float Dfull = 0.f;
       if constexpr (!kGivenD) {
         float Dother = 0.f;
@@ -631,31 +665,34 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
         Dfull = Dacc + Dother;
       }
       if (part < 0) {
-        if constexpr (kGivenD) {
+        // this row's kHalf outputs, packed to 16-bit as 16-byte chunks, then
+        // stored warp-coalesced
+        uint4 ch[kHalf / 8];
+        const float sD = kGivenD ? 0.f : Dfull - shift;
 #pragma unroll
-          for (int x = 0; x < kHalf / 32; ++x) {
-            uint32_t a[32];
-            __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
-                           // row-guarded stores of the previous iteration
-            tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
-            if (m < M) store_row_32<T>(out + 32 * x, reinterpret_cast<const float*>(a));
+        for (int x = 0; x < kHalf / 32; ++x) {
+          uint32_t a[32], bb[32];
+          __syncwarp();  // .sync.aligned TMEM access
+          tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
+          if constexpr (!kGivenD) tmem_load_32(lane_base + Cfg::kColB + c * kHalf + 32 * x, bb);
+#pragma unroll
+          for (int y = 0; y < 4; ++y) {
+            float v[8];
+#pragma unroll
+            for (int z = 0; z < 8; ++z)
+              v[z] = kGivenD ? __uint_as_float(a[8 * y + z])
+                             : fmaf(-sD, __uint_as_float(bb[8 * y + z]), __uint_as_float(a[8 * y + z]));
+            ch[4 * x + y] = make_uint4(Elem<T>::pack(v[0], v[1]), Elem<T>::pack(v[2], v[3]),
+                                       Elem<T>::pack(v[4], v[5]), Elem<T>::pack(v[6], v[7]));
           }
-        } else {
-          const float sD = Dfull - shift;
-#pragma unroll
-          for (int x = 0; x < kHalf / 32; ++x) {
-            uint32_t a[32], bb[32];
-            __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
-                           // row-guarded stores of the previous iteration
-            tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
-            tmem_load_32(lane_base + Cfg::kColB + c * kHalf + 32 * x, bb);
-            float v[32];
-#pragma unroll
-            for (int y = 0; y < 32; ++y) v[y] = fmaf(-sD, __uint_as_float(bb[y]), __uint_as_float(a[y]));
-            if (m < M) store_row_32<T>(out + 32 * x, v);
-          }
-          if (c == 0 && m < M) Dsum[static_cast<int64_t>(h) * M + m] = Dfull;
         }
+        {
+          const int row0 = m - lane;  // this warp's first row (query index)
+          store_rows_coalesced<kHalf / 8>(
+              ch, reinterpret_cast<uint8_t*>(dQ + (static_cast<int64_t>(h) * M + row0) * D + c * kHalf),
+              static_cast<size_t>(D) * sizeof(T), lane, M - row0);
+        }
+        if (!kGivenD && c == 0 && m < M) Dsum[static_cast<int64_t>(h) * M + m] = Dfull;
       } else {
         float* mine = part_ws + static_cast<size_t>(u - um.full) * kSlot;
 #pragma unroll
@@ -1221,7 +1258,6 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     // hand the accumulators back to the issuers
     if (!mbar_wait(&bar[kKbAcc], tc & 1, ctx, 53)) { ok = false; break; }
     const int r = qq * 32 + lane;
-    const int n = n0 + r;
     constexpr int kHalf = D / 2;
     constexpr size_t kSlot = static_cast<size_t>(2) * kTile * D;  // floats per workspace slot
     {
@@ -1232,7 +1268,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const uint32_t col = (which == 0 ? Cfg::kColdV : Cfg::kColdK) + c * kHalf;
-        T* out = (which == 0 ? dV : dK) + (static_cast<int64_t>(h) * N + n) * D + c * kHalf;
+        uint4 ch[kHalf / 8];  // a whole item's row, packed to 16-bit
 #pragma unroll
         for (int x = 0; x < kHalf / 32; ++x) {
           uint32_t v[32];
@@ -1240,7 +1276,13 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
                          // row-guarded stores of the previous iteration
           tmem_load_32(lane_base + col + x * 32, v);
           if (part < 0) {
-            if (n < N) store_row_32<T>(out + x * 32, reinterpret_cast<const float*>(v));
+#pragma unroll
+            for (int y = 0; y < 4; ++y)
+              ch[4 * x + y] = make_uint4(
+                  Elem<T>::pack(__uint_as_float(v[8 * y]), __uint_as_float(v[8 * y + 1])),
+                  Elem<T>::pack(__uint_as_float(v[8 * y + 2]), __uint_as_float(v[8 * y + 3])),
+                  Elem<T>::pack(__uint_as_float(v[8 * y + 4]), __uint_as_float(v[8 * y + 5])),
+                  Elem<T>::pack(__uint_as_float(v[8 * y + 6]), __uint_as_float(v[8 * y + 7])));
           } else {
             float4* dst = reinterpret_cast<float4*>(mine + (static_cast<size_t>(which) * kTile + r) * D +
                                                     c * kHalf + 32 * x);
@@ -1249,6 +1291,15 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
               dst[y] = make_float4(__uint_as_float(v[4 * y]), __uint_as_float(v[4 * y + 1]),
                                    __uint_as_float(v[4 * y + 2]), __uint_as_float(v[4 * y + 3]));
           }
+        }
+        if (part < 0) {
+          __syncwarp();
+          const int row0 = n0 + qq * 32;  // this warp's first row (key index)
+          store_rows_coalesced<kHalf / 8>(
+              ch,
+              reinterpret_cast<uint8_t*>((which == 0 ? dV : dK) + (static_cast<int64_t>(h) * N + row0) * D +
+                                         c * kHalf),
+              static_cast<size_t>(D) * sizeof(T), lane, N - row0);
         }
       }
       tc_fence_before();
