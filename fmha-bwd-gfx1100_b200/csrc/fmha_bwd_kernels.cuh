@@ -748,12 +748,13 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 // query), dV [256,256+D), dK [256+D,256+2D) (lane = key, column = d).
 //
 // Warp roles: 0 TMA for V_j and the P stream; 1 MMA issuer for dP^T (and
-// TMEM owner); 2 TMA for dO_i and Q_i; 3 MMA issuer for dV and, at D = 128,
-// dK; 4-11 dS warps (TMEM lane quarter = warp % 4, query half =
-// (warp - 4) / 4), which also write dK_j, dV_j; at D = 64, warp 12 issues dK.
-// At D = 64 each MMA group is short and a thread between two of its groups
-// spends a few hundred cycles on barrier waits and commits even when nothing
-// is outstanding, so three issuing threads keep the pipe fed better.
+// TMEM owner) and, at D = 128, dV; 2 TMA for dO_i and Q_i; 3 MMA issuer for
+// dK at D = 128, for dV at D = 64; 4-11 dS warps (TMEM lane quarter =
+// warp % 4, query half = (warp - 4) / 4), which also write dK_j, dV_j; at
+// D = 64, warp 12 issues dK. At D = 64 each MMA group is short and a thread
+// between two of its groups spends a few hundred cycles on barrier waits and
+// commits even when nothing is outstanding, so three issuing threads keep
+// the pipe fed better.
 template <int D>
 struct DkvCfg {
   static constexpr int kMD = (D / kBoxCols) * kBoxBytes;
@@ -772,8 +773,9 @@ struct DkvCfg {
   static constexpr int kSmemBytes = kTileBytes + kBarBytes + 1024;
   static constexpr int kDSWarps = 8;
   static constexpr int kFirstDSWarp = 4;
-  // D = 64: dV and dK have an issuing thread each (warps 3 and kDKWarp);
-  // D = 128: warp 3 issues both (at D = 128 the split measured slower).
+  // D = 128: warp 1 issues dP^T and dV (both read dO_i, so its ring slot
+  // is released once both are done), warp 3 issues dK. D = 64: warps 1, 3
+  // and kDKWarp issue dP^T, dV and dK.
   static constexpr bool kSplit = D == 64;
   static constexpr int kDKWarp = kFirstDSWarp + kDSWarps;  // dK issuer (D = 64)
   static constexpr int kThreads = 32 * (kDKWarp + (kSplit ? 1 : 0));
@@ -791,7 +793,7 @@ enum DkvBar : int {
   kKbPFull0 = 1,    // + slot (up to 3)
   kKbPEmpty0 = 4,   // + slot: dV commit + 8 dS warps
   kKbDOFull0 = 7,   // + slot (up to 4)
-  kKbDOEmpty0 = 11, // + slot: dP^T commit + dV commit
+  kKbDOEmpty0 = 11, // + slot: dP^T and dV commits (one commit after both at D = 128)
   kKbQFull0 = 15,   // + slot (up to 3)
   kKbQEmpty0 = 18,  // + slot
   kKbXFull0 = 21,   // + TMEM buffer (up to 3): dP^T_i computed
@@ -842,7 +844,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     }
     for (int s = 0; s < SD; ++s) {
       mbar_init(&bar[kKbDOFull0 + s], 1);
-      mbar_init(&bar[kKbDOEmpty0 + s], 2);
+      mbar_init(&bar[kKbDOEmpty0 + s], Cfg::kSplit ? 2 : 1);
     }
     for (int s = 0; s < SQ; ++s) {
       mbar_init(&bar[kKbQFull0 + s], 1);
@@ -853,7 +855,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       mbar_init(&bar[kKbEFull0 + s], kEpi);
       mbar_init(&bar[kKbXFree0 + s], 1);
     }
-    mbar_init(&bar[kKbAcc], Cfg::kSplit ? 2 : 1);
+    mbar_init(&bar[kKbAcc], 2);
     mbar_init(&bar[kKbDrain], 1);
     mbar_init(&bar[kKbDrain2], 1);
     mbar_init(&bar[kKbDrain3], 1);
@@ -1015,10 +1017,11 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     }
   } else if (warp == 1 || warp == 3 || warp == Cfg::kDKWarp) {
     // ---- MMA issuers (the others keep the tensor pipe fed while one waits).
-    // Warp 1: dP^T_i into TMEM buffer i % 2. Warp 3: dV_j += P^T dO_i, and
-    // at D = 128 also dK_j += dS^T Q_i in the order dV_0 dK_0 dV_1 dK_1 ...
-    // (dK_i first: it frees buffer i % 2 for dP^T_(i+2)); at D = 64 warp
-    // kDKWarp issues dK.
+    // Warp 1: dP^T_i into TMEM buffer i % NX, and at D = 128 dV_j += P^T
+    // dO_i right behind it (a dV issued after dK_(i-1), which waits for the
+    // dS warps, held dO_i's slot and with it dP^T_(i+2): 3.5 % more SM
+    // cycles at FLUX). D = 64: warp 3 issues dV. dK_j += dS^T Q_i: warp 3
+    // at D = 128, kDKWarp at D = 64.
     if (lane == 0) {
       constexpr bool kB = Elem<T>::kBF16;
       constexpr uint32_t id_dP = make_idesc_f16<kB>(kTile, kTile, false, false);
@@ -1047,70 +1050,34 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
                         k > 0 ? 1u : 0u);
           }
           umma_commit(&bar[kKbXFull0 + x]);
+          if constexpr (!Cfg::kSplit) {
+            // dV_j += P_ij^T dO_i : A = P^T (MN-major, M = key), B = dO_i
+            // (MN-major, N = d); the accumulator must have been read out
+            const int sp = g % SP;
+            if (i == lo && tc > 0 && !mbar_wait(&bar[kKbAccEmpty], (tc - 1) & 1, ctx, 47)) { ok = false; break; }
+            if (!mbar_wait(&bar[kKbPFull0 + sp], (g / SP) & 1, ctx, 42)) { ok = false; break; }
+            tc_fence_after();
+            const uint64_t ddOm = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD), kBoxBytes, 1024);
+            const uint64_t dP = make_sw128_desc(smem_u32(smem + Cfg::kOffP + sp * Cfg::kPT), kBoxBytes, 1024);
+#pragma unroll
+            for (int k = 0; k < kTile / 16; ++k) {
+              umma_f16_ss(tmem + Cfg::kColdV, desc_advance(dP, k * 2048), desc_advance(ddOm, k * 2048), id_dV,
+                          (i > lo || k > 0) ? 1u : 0u);
+            }
+            umma_commit(&bar[kKbPEmpty0 + sp]);
+          }
           umma_commit(&bar[kKbDOEmpty0 + s]);
         }
-        if (ok) umma_commit(&bar[kKbVEmpty]);  // V_j consumed
+        if (ok) {
+          umma_commit(&bar[kKbVEmpty]);             // V_j consumed
+          if (!Cfg::kSplit) umma_commit(&bar[kKbAcc]);  // dV complete
+        }
         }
         if (!ok) {
           umma_commit(&bar[kKbDrain]);
           mbar_wait_drain(&bar[kKbDrain], 0, timeout_ns);
         }
-      } else if (warp == 3 && !Cfg::kSplit) {
-        auto issue_dV = [&](bool first, int g) -> bool {
-          const int sp = g % SP, sd = g % SD;
-          const uint64_t ddO = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + sd * Cfg::kMD), kBoxBytes, 1024);
-          const uint64_t dP = make_sw128_desc(smem_u32(smem + Cfg::kOffP + sp * Cfg::kPT), kBoxBytes, 1024);
-          // dV += P_ij^T dO_i : A = P^T (MN-major, M = key), B = dO_i (MN-major, N = d).
-          if (!mbar_wait(&bar[kKbPFull0 + sp], (g / SP) & 1, ctx, 42)) return false;
-          if (!mbar_wait(&bar[kKbDOFull0 + sd], (g / SD) & 1, ctx, 46)) return false;
-          tc_fence_after();
-#pragma unroll
-          for (int k = 0; k < kTile / 16; ++k) {
-            umma_f16_ss(tmem + Cfg::kColdV, desc_advance(dP, k * 2048), desc_advance(ddO, k * 2048), id_dV,
-                        (!first || k > 0) ? 1u : 0u);
-          }
-          umma_commit(&bar[kKbDOEmpty0 + sd]);
-          umma_commit(&bar[kKbPEmpty0 + sp]);
-          return true;
-        };
-        auto issue_dK = [&](bool first, int g) -> bool {
-          const int s = g % SQ;
-          const uint64_t dQd = make_sw128_desc(smem_u32(smem + Cfg::kOffQ + s * Cfg::kMD), kBoxBytes, 1024);
-          // dK += dS^T Q_i : A = dS^T from TMEM buffer g % NX (16 queries =
-          // 8 packed columns per step), B = Q_i (MN-major, N = d).
-          if (!mbar_wait(&bar[kKbQFull0 + s], (g / SQ) & 1, ctx, 43)) return false;
-          if (!mbar_wait(&bar[kKbEFull0 + g % NX], (g / NX) & 1, ctx, 44)) return false;
-          tc_fence_after();
-          const uint32_t tS = tmem + Cfg::kColX + 128 * (g % NX);
-#pragma unroll
-          for (int k = 0; k < kTile / 16; ++k) {
-            umma_f16_ts(tmem + Cfg::kColdK, tS + (k >> 2) * 64 + (k & 3) * 8,
-                        desc_advance(dQd, k * 2048), id_dK, (!first || k > 0) ? 1u : 0u);
-          }
-          umma_commit(&bar[kKbQEmpty0 + s]);
-          umma_commit(&bar[kKbXFree0 + g % NX]);
-          return true;
-        };
-        int g = 0, tc = 0;
-        for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
-          int t, lo, hi, part;
-          um.get(u, mt, t, lo, hi, part);
-          const int n = hi - lo;
-          // dV and dK of the previous unit must have been read out first
-          if (tc > 0 && !mbar_wait(&bar[kKbAccEmpty], (tc - 1) & 1, ctx, 47)) { ok = false; break; }
-          ok = issue_dV(true, g);
-          for (int i = 0; i < n && ok; ++i) {
-            if (!issue_dK(i == 0, g + i)) { ok = false; break; }
-            if (i + 1 < n && !issue_dV(false, g + i + 1)) { ok = false; break; }
-          }
-          g += n;
-          if (ok) umma_commit(&bar[kKbAcc]);
-        }
-        if (!ok) {
-          umma_commit(&bar[kKbDrain2]);
-          mbar_wait_drain(&bar[kKbDrain2], 0, timeout_ns);
-        }
-      } else if (warp == 3) {
+      } else if (warp == 3 && Cfg::kSplit) {
         int g = 0, tc = 0;
         for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
           int t, lo, hi, part;
