@@ -356,17 +356,27 @@ __global__ void __launch_bounds__(DqLseCfg<D>::kThreads, 1)
       __syncwarp();
       tc_fence_after();
       constexpr int kHalf = D / 2;
-      T* out = dQ + (static_cast<int64_t>(h) * M + m) * D + c * kHalf;
+      // this row's outputs packed to 16-bit as 16-byte chunks, then stored
+      // warp-coalesced
+      uint4 ch[kHalf / 8];
 #pragma unroll
       for (int x = 0; x < kHalf / 32; ++x) {
         uint32_t a[32];
-        __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
-                       // row-guarded stores of the previous iteration
+        __syncwarp();  // .sync.aligned TMEM access
         tmem_load_32(lane_base + Cfg::kColA + c * kHalf + 32 * x, a);
-        float v[32];
 #pragma unroll
-        for (int y = 0; y < 32; ++y) v[y] = scale * __uint_as_float(a[y]);
-        if (m < M) store_row_32<T>(out + 32 * x, v);
+        for (int y = 0; y < 4; ++y)
+          ch[4 * x + y] = make_uint4(
+              Elem<T>::pack(scale * __uint_as_float(a[8 * y]), scale * __uint_as_float(a[8 * y + 1])),
+              Elem<T>::pack(scale * __uint_as_float(a[8 * y + 2]), scale * __uint_as_float(a[8 * y + 3])),
+              Elem<T>::pack(scale * __uint_as_float(a[8 * y + 4]), scale * __uint_as_float(a[8 * y + 5])),
+              Elem<T>::pack(scale * __uint_as_float(a[8 * y + 6]), scale * __uint_as_float(a[8 * y + 7])));
+      }
+      {
+        const int row0 = m - lane;  // this warp's first row (query index)
+        store_rows_coalesced<kHalf / 8>(
+            ch, reinterpret_cast<uint8_t*>(dQ + (static_cast<int64_t>(h) * M + row0) * D + c * kHalf),
+            static_cast<size_t>(D) * sizeof(T), lane, M - row0);
       }
       tc_fence_before();
       __syncwarp();
@@ -757,26 +767,34 @@ __global__ void __launch_bounds__(DkvLseCfg<D>::kThreads, 1)
       if (!mbar_wait(&bar[kLkAcc], tc & 1, ctx, 172)) { ok = false; break; }
       __syncwarp();
       tc_fence_after();
-      const int r = qq * 32 + lane;
       const uint32_t lane_base = tmem + (static_cast<uint32_t>(qq * 32) << 16);
-      const int n = n0 + r;
       constexpr int kHalf = D / 2;
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const uint32_t col = (which == 0 ? Cfg::kColdV : Cfg::kColdK) + c * kHalf;
         const float mul = which == 0 ? 1.f : scale;
-        T* out = (which == 0 ? dV : dK) + (static_cast<int64_t>(h) * N + n) * D + c * kHalf;
+        uint4 ch[kHalf / 8];  // this row, packed to 16-bit, stored warp-coalesced
 #pragma unroll
         for (int x = 0; x < kHalf / 32; ++x) {
           uint32_t v[32];
           __syncwarp();  // .sync.aligned TMEM access: the warp reconverges after the
                          // row-guarded stores of the previous iteration
           tmem_load_32(lane_base + col + x * 32, v);
-          float f[32];
 #pragma unroll
-          for (int y = 0; y < 32; ++y) f[y] = mul * __uint_as_float(v[y]);
-          if (n < N) store_row_32<T>(out + x * 32, f);
+          for (int y = 0; y < 4; ++y)
+            ch[4 * x + y] = make_uint4(
+                Elem<T>::pack(mul * __uint_as_float(v[8 * y]), mul * __uint_as_float(v[8 * y + 1])),
+                Elem<T>::pack(mul * __uint_as_float(v[8 * y + 2]), mul * __uint_as_float(v[8 * y + 3])),
+                Elem<T>::pack(mul * __uint_as_float(v[8 * y + 4]), mul * __uint_as_float(v[8 * y + 5])),
+                Elem<T>::pack(mul * __uint_as_float(v[8 * y + 6]), mul * __uint_as_float(v[8 * y + 7])));
         }
+        __syncwarp();
+        const int row0 = n0 + qq * 32;  // this warp's first row (key index)
+        store_rows_coalesced<kHalf / 8>(
+            ch,
+            reinterpret_cast<uint8_t*>((which == 0 ? dV : dK) + (static_cast<int64_t>(h) * N + row0) * D +
+                                       c * kHalf),
+            static_cast<size_t>(D) * sizeof(T), lane, N - row0);
       }
       tc_fence_before();
       __syncwarp();
