@@ -184,25 +184,38 @@ inline bool ensure_status_slot(int device, DeviceWorkspace& w) {
   return true;
 }
 
-// Work units for `items` items of `len` steps each on `grid` CTAs: when the
-// last wave would be at most half full, its items are split into 2..4 parts
-// that fill one wave. Items shorter than kMinSplitLen steps stay whole: a
-// part carries fixed costs (its first operand tiles, the readout of fp32
-// partials, a share of the combine kernel). Splitting needs a partial-sum
-// workspace; without one (`allow` false) every item stays whole.
+// Work units for `items` items of `len` steps each on `grid` CTAs. The
+// items fill `items / grid` whole waves; the `tail` left over would run as
+// one partly filled wave. Splitting each tail item into q parts (q <= 4,
+// parts of at least 8 steps) runs the tail as ceil(q tail / grid) waves of
+// parts 1/q as long, so the tail costs ceil(q tail / grid) / q item times
+// instead of one; the q with the lowest cost is taken when it saves at least
+// a tenth of an item time (a part carries fixed costs: its first operand
+// tiles, the readout of fp32 partials, a share of the combine kernel).
+// Items shorter than kMinSplitLen steps stay whole. Examples on 148 CTAs:
+// 192 items (a tail of 44) -> 3 parts, one wave of parts, 1/3 of an item
+// time; 1280 items (tail 96) -> 3 parts, two waves of parts, 2/3; 864 items
+// (tail 124) -> no split. Splitting needs a partial-sum workspace; without
+// one (`allow` false) every item stays whole.
 constexpr int kMinSplitLen = 16;
 inline UnitMap plan_units(int items, int grid, int len, bool allow) {
   UnitMap um{items, 1, items};
   if (!allow || grid <= 0 || len < kMinSplitLen) return um;
   const int waves = items / grid, tail = items - waves * grid;
-  if (tail == 0 || 2 * tail > grid) return um;
-  int q = grid / tail;
-  q = q < 4 ? q : 4;
-  q = q < len / 2 ? q : len / 2;
-  if (q < 2) return um;
+  if (tail == 0) return um;
+  int best_q = 1;
+  double best = 1.0;
+  for (int q = 2; q <= kMaxParts && len / q >= 8; ++q) {
+    const double cost = static_cast<double>((q * tail + grid - 1) / grid) / q;
+    if (cost < best - 0.1) {
+      best = cost;
+      best_q = q;
+    }
+  }
+  if (best_q == 1) return um;
   um.full = waves * grid;
-  um.parts = q;
-  um.units = um.full + q * tail;
+  um.parts = best_q;
+  um.units = um.full + best_q * tail;
   return um;
 }
 

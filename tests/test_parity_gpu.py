@@ -304,17 +304,19 @@ def test_extreme_shapes(F, oracle_built, M, N, d, H, name):
 
 @pytest.mark.parametrize("M,N,d,H,dtype", [(8192, 256, 128, 20, "bf16"), (8192, 384, 64, 13, "fp16"),
                                           (8200, 128, 128, 37, "bf16"), (256, 8192, 128, 20, "bf16"),
-                                          (200, 8200, 64, 30, "fp16")])
+                                          (200, 8200, 64, 30, "fp16"), (8192, 1024, 128, 30, "bf16"),
+                                          (1000, 8192, 64, 30, "fp16")])
 def test_tail_items_split_into_parts(F, oracle_built, M, N, d, H, dtype):
-    """Long items (64 or more steps) of a last, at most half-full wave are
-    split into 2-4 parts whose fp32 partials the last part to finish adds up:
-    the dK/dV kernel's key-tile items over the query tiles (M >= 8192, 37-40
-    items on 148 SMs), and the dQ kernel's query-tile items over the key tiles
-    (N >= 8192: partial A, B, rowsum and shift per part, dQ = sum_p A_p -
-    (D - c_p) B_p); ragged M and N included. NaN-prefilled outputs must be
-    fully written, repeated calls must agree bit for bit (the part counters
-    reset themselves), and every head must match the fp32 recompute; two
-    heads also the CPU oracle."""
+    """The items of a kernel's partly filled last wave are split into 2-4
+    parts (on 148 SMs) whose fp32 partials a combine kernel adds up after
+    the main kernel: the dK/dV kernel's key-tile items over the query tiles
+    (M >= 8192: 37-40 items, one wave of parts; 240 items, a tail of 92 run
+    as two waves of thirds), and the dQ kernel's query-tile items over the
+    key tiles (N >= 8192: partial A, B, rowsum and shift per part,
+    dQ = sum_p A_p - (D - c_p) B_p; 240 items at 1000 x 8192); ragged M and N
+    included. NaN-prefilled outputs must be fully written, repeated calls
+    must agree bit for bit, and every head must match the fp32 recompute;
+    two heads also the CPU oracle."""
     O = oracle_built
     Qb, Kb, Vb, Pb, dOb = O.make_inputs(M, N, d, H, dtype, seed=21)
     dt = _dt(dtype)
