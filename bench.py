@@ -234,7 +234,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="flux")
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=2048,
                     help="query rows per head in the CPU baseline sample (0: all M rows); "
@@ -358,37 +358,72 @@ def main() -> int:
     value = total_flops / (ms_max * 1e-3) / 1e12
     ms_per_step = ms_max / K_steps
 
-    # ---- e2e through the reference-facing call with host buffers
+    # ---- e2e through the reference-facing call with host buffers. Every
+    # step copies its inputs from pinned host memory, runs the synchronous
+    # reference-facing call and copies its results back; steps are
+    # pipelined as a user would: step k+1's inputs upload (copy stream, into
+    # the other of two device input sets) while step k computes, and step
+    # k's results download (a second copy stream, PCIe is full duplex) while
+    # step k+1's inputs upload.
     e2e = None
     if args.e2e_steps > 0:
         hQ, hK, hV, hP, hdO = (t.cpu().pin_memory() for t in (Q, K, V, P, dO))
+        hin = (hQ, hK, hV, hP, hdO)
         ohQ, ohK, ohV = (torch.empty_like(t, device="cpu").pin_memory() for t in (Q, K, V))
-        dQ2, dK2, dV2 = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
-        dev_in = [torch.empty_like(t) for t in (Q, K, V, P, dO)]
-        h2d = sum(t.numel() * t.element_size() for t in (hQ, hK, hV, hP, hdO))
+        dev_in = [[torch.empty_like(t) for t in (Q, K, V, P, dO)] for _ in range(2)]
+        dev_out = [[torch.empty_like(t) for t in (Q, K, V)] for _ in range(2)]
+        h2d = sum(t.numel() * t.element_size() for t in hin)
         d2h = sum(t.numel() * t.element_size() for t in (ohQ, ohK, ohV))
         full = lib.fmha_bwd_full_py if w.dtype == "bf16" else lib.fmha_bwd_full_fp16
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        main = torch.cuda.current_stream(dev)
 
-        def e2e_step():
-            for dst, src in zip(dev_in, (hQ, hK, hV, hP, hdO)):
-                dst.copy_(src, non_blocking=True)
-            full(dQ2.data_ptr(), dK2.data_ptr(), dV2.data_ptr(),
-                 *(t.data_ptr() for t in dev_in), w.M, w.N, w.d, heads)
-            for dst, src in zip((ohQ, ohK, ohV), (dQ2, dK2, dV2)):
-                dst.copy_(src, non_blocking=True)
+        def upload(k):
+            with torch.cuda.stream(s_in):
+                for dst, src in zip(dev_in[k % 2], hin):
+                    dst.copy_(src, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(s_in)
+            return ev
 
-        e2e_step()
+        def e2e_run(n_steps):
+            ev_in = upload(0)
+            ev_out = [None, None]
+            for k in range(n_steps):
+                main.wait_event(ev_in)
+                if ev_out[k % 2] is not None:
+                    main.wait_event(ev_out[k % 2])  # step k-2's download done
+                if k + 1 < n_steps:
+                    ev_in = upload(k + 1)
+                o, i = dev_out[k % 2], dev_in[k % 2]
+                full(*(t.data_ptr() for t in o), *(t.data_ptr() for t in i), w.M, w.N, w.d, heads)
+                done = torch.cuda.Event()
+                done.record(main)
+                s_out.wait_event(done)
+                with torch.cuda.stream(s_out):
+                    for dst, src in zip((ohQ, ohK, ohV), o):
+                        dst.copy_(src, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(s_out)
+                ev_out[k % 2] = ev
+            for ev in ev_out:
+                if ev is not None:
+                    main.wait_event(ev)
+
+        e2e_run(2)
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
         s0 = torch.cuda.Event(enable_timing=True)
         s1 = torch.cuda.Event(enable_timing=True)
-        s0.record()
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        s1.record()
+        s0.record(main)
+        s_in.wait_stream(main)
+        s_out.wait_stream(main)
+        e2e_run(args.e2e_steps)
+        s1.record(main)
         torch.cuda.synchronize(dev)
         e2e_ms = s0.elapsed_time(s1)
+        dQ2, dK2, dV2 = dev_out[(args.e2e_steps - 1) % 2]
         if lib.fmha_bwd_last_error() != 0:
             raise RuntimeError(lib.fmha_bwd_last_error_message().decode())
         # the host->device copies alone: this rank's pinned-host copy rate
@@ -396,7 +431,7 @@ def main() -> int:
         c1 = torch.cuda.Event(enable_timing=True)
         c0.record()
         for _ in range(3):
-            for dst, src in zip(dev_in, (hQ, hK, hV, hP, hdO)):
+            for dst, src in zip(dev_in[0], hin):
                 dst.copy_(src, non_blocking=True)
         c1.record()
         torch.cuda.synchronize(dev)
@@ -411,12 +446,13 @@ def main() -> int:
                "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": e2e_ms / args.e2e_steps,
                "h2d_gbs_per_rank": h2d_rank,
-               "note": "host copies dominate: every rank's pinned buffers sit in one host's "
-                       "memory, so the per-rank copy rate falls as ranks are added",
+               "note": "host copies dominate (steps pipelined: uploads overlap the previous "
+                       "step's compute and download); every rank's pinned buffers sit in one "
+                       "host's memory, so the per-rank copy rate falls as ranks are added",
                "entry": "fmha_bwd_full_py" if w.dtype == "bf16" else "fmha_bwd_full_fp16"}
         if not torch.equal(dK2, dK) or not torch.equal(dV2, dV):
             raise RuntimeError("e2e outputs differ from the device-resident run")
-        del hQ, hK, hV, hP, hdO, ohQ, ohK, ohV, dQ2, dK2, dV2, dev_in
+        del hQ, hK, hV, hP, hdO, hin, ohQ, ohK, ohV, dQ2, dK2, dV2, dev_in, dev_out
 
     # ---- strong scaling: the long video workload's 40 heads split over the
     # ranks (workloads.head_range: 40/20/10/5 heads per GPU at 1/2/4/8 GPUs),
