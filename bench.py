@@ -171,6 +171,30 @@ def cpu_reference_sample(w, rows: int, threads: int, seed: int = 42):
     return 8.0 * rows * w.N * w.d * threads, dt, kind, threads
 
 
+def launches_per_call(w, heads: int, sms: int) -> int:
+    """Kernels one backward call launches: dq_kernel and dkv_kernel, each
+    followed by its combine kernel when the library splits its tail items
+    (the library's work-unit rule: items of 16+ steps; the tail split into
+    q <= 4 parts of 8+ steps when that saves a tenth of an item time)."""
+    def split(items: int, length: int) -> bool:
+        if length < 16:
+            return False
+        tail = items % sms
+        if tail == 0:
+            return False
+        best_q, best = 1, 1.0
+        for q in range(2, 5):
+            if length // q < 8:
+                break
+            cost = ((q * tail + sms - 1) // sms) / q
+            if cost < best - 0.1:
+                best, best_q = cost, q
+        return best_q > 1
+
+    mt, nt = -(-w.M // 128), -(-w.N // 128)
+    return 2 + int(split(mt * heads, nt)) + int(split(nt * heads, mt))
+
+
 def cpu_threads(w) -> int:
     n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     return max(1, min(n, w.heads))
@@ -622,7 +646,8 @@ def main() -> int:
         "e2e": e2e,
         "strong": strong,
         "recompute_p": recompute_p,
-        "gpu_launches": 2 * K_steps,
+        "gpu_launches": launches_per_call(
+            w, heads, torch.cuda.get_device_properties(dev).multi_processor_count) * K_steps,
         "roofline": roofline,
         "clocks": clocks,
         "checksums": checksums,
