@@ -97,8 +97,7 @@ FMHA_API int fmha_bwd_full_stream_events(bf16* dQ, bf16* dK, bf16* dV, const bf1
 // fmha_bwd_full_stream, plus total_heads * M <= kNoAllocMaxRows; allocates
 // nothing. Enqueues on `stream`, waits for it, and returns 0 or an error code.
 // The first call on a device looks up the scratch arrays' addresses (module
-// load included); that first call should come before any stream capture.
-// Every call shares the one scratch: calls that overlap on the GPU (other
+// load included). Every call shares the one scratch: calls that overlap on the GPU (other
 // streams, other host threads) race.
 FMHA_API int fmha_bwd_full_noalloc(bf16* dQ, bf16* dK, bf16* dV, const bf16* Q, const bf16* K,
                                    const bf16* V, const bf16* P, const bf16* dO, int M, int N,

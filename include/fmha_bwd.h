@@ -125,8 +125,8 @@ int fmha_bwd_full_lse(fmha_bf16_t* dQ, fmha_bf16_t* dK, fmha_bf16_t* dV,
  * launch. Enqueues on `stream`, waits for that stream and returns 0 or an
  * error code (in-kernel wait timeouts included). The first call on a device
  * looks up the scratch addresses (cudaGetSymbolAddress, which loads the
- * module); make that first call before any stream capture. All calls share
- * the one scratch: calls that overlap on the GPU race. */
+ * module). All calls share the one scratch: calls that overlap on the GPU
+ * race. */
 int fmha_bwd_full_noalloc(fmha_bf16_t* dQ, fmha_bf16_t* dK, fmha_bf16_t* dV,
                           const fmha_bf16_t* Q, const fmha_bf16_t* K,
                           const fmha_bf16_t* V, const fmha_bf16_t* P,
