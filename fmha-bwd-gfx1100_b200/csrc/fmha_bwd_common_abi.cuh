@@ -15,6 +15,17 @@ FMHA_API int fmha_bwd_last_error(void) { return fmha_sm100::error_state().code.l
 
 FMHA_API const char* fmha_bwd_last_error_message(void) { return fmha_sm100::error_state().message; }
 
+FMHA_API int fmha_bwd_work_units(int items, int grid, int len, int allow, int* out) {
+  using namespace fmha_sm100;
+  if (!out || items < 0 || grid < 0 || len < 0)
+    return set_error(kErrInvalidArgument, "work_units: null out or negative size");
+  const UnitMap um = plan_units(items, grid, len, allow != 0);
+  out[0] = um.full;
+  out[1] = um.parts;
+  out[2] = um.units;
+  return kOk;
+}
+
 FMHA_API int fmha_bwd_poll_device_status(void) {
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) {

@@ -242,6 +242,16 @@ int fmha_bwd_poll_device_status(void);
  * context stays usable); otherwise an error code. Synchronises the device. */
 int fmha_bwd_selftest_wait_timeout(int timeout_ms);
 
+/* No counterpart in the reference. Host-only, launches nothing: how a call
+ * divides `items` work items of `len` steps each (query tiles for the dQ
+ * kernel, key tiles for the dK/dV kernel, times total_heads) over `grid`
+ * persistent CTAs. out[0] = items run whole, out[1] = parts each remaining
+ * (tail) item is split into (1: none), out[2] = work units in all; a split
+ * kernel is followed by a combine kernel. `allow` = 0 reports the plan of a
+ * call without a partial-sum workspace (never split). Returns FMHA_BWD_OK,
+ * or FMHA_BWD_ERR_INVALID_ARGUMENT for a null `out` or negative sizes. */
+int fmha_bwd_work_units(int items, int grid, int len, int allow, int* out);
+
 /* Upper bound, in milliseconds, on any single in-kernel wait (default 4000,
  * or FMHA_BWD_WAIT_TIMEOUT_MS). A wait that runs out sets the device status
  * word and the kernel drains and exits instead of hanging. 0 restores the
