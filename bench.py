@@ -14,7 +14,9 @@ Reported (one JSON line from rank 0):
   value       counted TFLOP/s (8*M*N*d*heads, all ranks) / max-over-ranks
               device time of K back-to-back steps, inputs resident in HBM
               (P alone is 1.02 GB per GPU, far larger than the 126 MB L2, so
-              no L2 flush is needed between steps)
+              no L2 flush is needed between steps; alternate steps also use
+              two copies of the inputs, so no step starts on rows the step
+              before it left in L2)
   e2e         the same metric through the reference-facing C-ABI call
               (fmha_bwd_full_py) with host buffers: pinned-host -> device
               copies of Q, K, V, P, dO and device -> host copies of dQ, dK, dV
@@ -310,18 +312,23 @@ def main() -> int:
                                                                    ctypes.c_void_p]
     ev_fn.restype = ctypes.c_int
     stream = torch.cuda.Stream(device=dev)
-    ptrs = (dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), Q.data_ptr(), K.data_ptr(),
-            V.data_ptr(), P.data_ptr(), dO.data_ptr(), w.M, w.N, w.d, heads)
+    # two copies of the inputs and outputs, used by alternate steps, so that
+    # no step starts on rows the step before it left in L2
+    sets = [(Q, K, V, P, dO, dQ, dK, dV),
+            tuple(t.clone() for t in (Q, K, V, P, dO)) +
+            tuple(torch.empty_like(t) for t in (dQ, dK, dV))]
+    ptrs = [(s[5].data_ptr(), s[6].data_ptr(), s[7].data_ptr(), s[0].data_ptr(), s[1].data_ptr(),
+             s[2].data_ptr(), s[3].data_ptr(), s[4].data_ptr(), w.M, w.N, w.d, heads) for s in sets]
 
-    def step(events_arr=None):
-        rc = ev_fn(*ptrs, ctypes.c_void_p(stream.cuda_stream),
+    def step(events_arr=None, k=0):
+        rc = ev_fn(*ptrs[k % 2], ctypes.c_void_p(stream.cuda_stream),
                    ctypes.cast(events_arr, ctypes.c_void_p) if events_arr is not None else None)
         if rc != 0:
             raise F.FmhaBwdError(rc, lib.fmha_bwd_last_error_message().decode())
 
     torch.cuda.synchronize(dev)
-    for _ in range(args.warmup):
-        step()
+    for k in range(args.warmup):
+        step(k=k)
     stream.synchronize()
     if lib.fmha_bwd_poll_device_status() != 0:
         raise RuntimeError("device status reported a wait timeout during warm-up")
@@ -352,7 +359,7 @@ def main() -> int:
     sampler.start()
     start.record(stream)
     for k in range(K_steps):
-        step(ev_arrays[k])
+        step(ev_arrays[k], k)
     end.record(stream)
     torch.cuda.synchronize(dev)
     if world > 1:
@@ -642,7 +649,8 @@ def main() -> int:
         "config": {"workload": w.description, "M": w.M, "N": w.N, "d": w.d,
                    "heads_per_gpu": heads, "total_heads": heads * world,
                    "parallelism": f"head-sharded x{world}, no data-path collective",
-                   "l2": "inputs larger than L2 (P is 1.02 GB per GPU vs 126 MB L2); no flush"},
+                   "l2": "inputs larger than L2 (P is 1.02 GB per GPU vs 126 MB L2), and "
+                         "alternate steps use two copies of the inputs; no flush"},
         "e2e": e2e,
         "strong": strong,
         "recompute_p": recompute_p,

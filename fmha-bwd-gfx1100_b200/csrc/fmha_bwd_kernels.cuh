@@ -731,8 +731,12 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 }
 
 // =============================================================== dkv_kernel
-// One CTA per (128-row key tile j, head), walking the query tiles i. The
-// transposed products keep the key index on the TMEM lanes:
+// One CTA per (128-row key tile j, head), walking the query tiles i. Items
+// take the heads from the last to the first (item t: head H - 1 - t / tiles):
+// dq_kernel, which runs just before on the same stream, takes them from the
+// first to the last, so the first waves here read the P and dO rows that it
+// read last, while they are still in L2. The transposed products keep the
+// key index on the TMEM lanes:
 //   dP_ij^T = V_j dO_i^T             (A = V_j, B = dO_i, both K-major over d)
 //   dS_ij^T = P_ij^T (dP_ij^T - D_i) (dS warps; written back into TMEM, 16-bit)
 //   dV_j  += P_ij^T dO_i             (A = P^T, B = dO_i, both MN-major)
@@ -889,8 +893,9 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x) {
         int t, lo, hi, part;
         um.get(u, mt, t, lo, hi, part);
-        const int h = t / ntk;
-        const int n0 = (t - h * ntk) * kTile;
+        const int hl = t / ntk;
+        const int n0 = (t - hl * ntk) * kTile;
+        const int h = H - 1 - hl;
         for (int i = lo; i < lo + kAhead && i < hi; ++i) {
           tma_prefetch_l2_3d(&tm_P, n0, i * kTile, h);
           tma_prefetch_l2_3d(&tm_P, n0 + kBoxCols, i * kTile, h);
@@ -944,7 +949,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           um.get(u, mt, t, lo, hi, part);
           c.i = lo;
           c.hi = hi;
-          c.h = t / ntk;
+          c.h = H - 1 - t / ntk;
         }
       };
       auto advance = [&](Cursor& c) {
@@ -1152,8 +1157,9 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
     int t, lo, hi, part;
     um.get(u, mt, t, lo, hi, part);
-    const int h = t / ntk;
-    const int n0 = (t - h * ntk) * kTile;
+    const int hl = t / ntk;
+    const int n0 = (t - hl * ntk) * kTile;
+    const int h = H - 1 - hl;
     for (int i = lo; i < hi; ++i, ++g) {
       const int s = g % SP;  // P slot of this step
       // D for this thread's 16 queries (rows of the query tile past M read 0)
@@ -1379,8 +1385,9 @@ __global__ void __launch_bounds__(kCombineThreads)
   const int64_t k = row / (2 * kTile);
   if (k >= tail) return;
   const int item = um.full + static_cast<int>(k);
-  const int h = item / ntk;
-  const int n = (item - h * ntk) * kTile + r;
+  const int hl = item / ntk;
+  const int n = (item - hl * ntk) * kTile + r;
+  const int h = (um.full + tail) / ntk - 1 - hl;  // heads last to first, as in dkv_kernel
   if (n >= N) return;
   const float* src = part_ws + static_cast<size_t>(k) * um.parts * kSlot +
                      (static_cast<size_t>(which) * kTile + r) * D + 8 * x;
