@@ -339,7 +339,9 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
       tma_prefetch_desc(&tm_dO);
       const uint64_t pol_p = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();
-      constexpr int kAhead = 4;  // P tiles pulled into L2 ahead of the ring
+      // No L2 prefetch ahead of the rings: prefetch requests share the TMA
+      // unit and L2 queues with the loads, and with them every kernel took
+      // 3-7 % more SM cycles.
       int g = 0, nV = 0, nP = 0, nK = 0, nD = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x) {
@@ -347,11 +349,6 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
         um.get(u, nt, t, lo, hi, part);
         const int h = t / mt;
         const int m0 = (t - h * mt) * kTile;
-        auto prefetch = [&](int j) {
-          tma_prefetch_l2_3d(&tm_P, j * kTile, m0, h);
-          tma_prefetch_l2_3d(&tm_P, j * kTile + kBoxCols, m0, h);
-        };
-        for (int j = lo; j < lo + kAhead && j < hi; ++j) prefetch(j);
         if (nD > 0 && !mbar_wait(&bar[kQbDOEmpty], (nD - 1) & 1, ctx, 4)) { ok = false; break; }
         mbar_arrive_expect_tx(&bar[kQbDO], Cfg::kMD);
 #pragma unroll
@@ -359,7 +356,6 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
           tma_load_3d(smem + Cfg::kOffdO + b * kBoxBytes, &tm_dO, &bar[kQbDO], b * kBoxCols, m0, h, pol_kv);
         ++nD;
         for (int j = lo; j < hi; ++j, ++g) {
-          if (j + kAhead < hi) prefetch(j + kAhead);
           if (g >= SV && !mbar_wait(&bar[kQbVEmpty0 + g % SV], ((g / SV) - 1) & 1, ctx, 1)) { ok = false; break; }
           {
             uint64_t* fb = &bar[kQbVFull0 + g % SV];
@@ -887,7 +883,6 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       tma_prefetch_desc(&tm_P);
       const uint64_t pol_p = l2_policy_evict_first();
       const uint64_t pol_v = l2_policy_evict_normal();
-      constexpr int kAhead = 4;  // P tiles pulled into L2 ahead of the 2-slot ring
       int g = 0, issued = 0, nv = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x) {
@@ -896,10 +891,6 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         const int hl = t / ntk;
         const int n0 = (t - hl * ntk) * kTile;
         const int h = H - 1 - hl;
-        for (int i = lo; i < lo + kAhead && i < hi; ++i) {
-          tma_prefetch_l2_3d(&tm_P, n0, i * kTile, h);
-          tma_prefetch_l2_3d(&tm_P, n0 + kBoxCols, i * kTile, h);
-        }
         if (nv > 0 && !mbar_wait(&bar[kKbVEmpty], (nv - 1) & 1, ctx, 32)) { ok = false; break; }
         mbar_arrive_expect_tx(&bar[kKbV], Cfg::kMD);
 #pragma unroll
@@ -909,10 +900,6 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
         for (int i = lo; i < hi; ++i, ++g) {
           const int s = g % SP;
           const int r = g / SP;
-          if (i + kAhead < hi) {
-            tma_prefetch_l2_3d(&tm_P, n0, (i + kAhead) * kTile, h);
-            tma_prefetch_l2_3d(&tm_P, n0 + kBoxCols, (i + kAhead) * kTile, h);
-          }
           if (r > 0 && !mbar_wait(&bar[kKbPEmpty0 + s], (r - 1) & 1, ctx, 30)) { ok = false; break; }
           uint8_t* dst = smem + Cfg::kOffP + s * Cfg::kPT;
           mbar_arrive_expect_tx(&bar[kKbPFull0 + s], Cfg::kPT);
@@ -930,15 +917,14 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
   } else if (warp == 2) {
     // ---- TMA producer for the L2-resident operands dO_i and Q_i (two slots
     // each; every key-tile CTA of the head reads them). Polls both "empty"
-    // barriers without blocking and issues whichever load can go; tiles are
-    // prefetched into L2 kL2Ahead query tiles ahead.
+    // barriers without blocking and issues whichever load can go (no L2
+    // prefetch ahead, as in the other producers).
     if (lane == 0) {
-      constexpr int kL2Ahead = 3;
       tma_prefetch_desc(&tm_dO);
       tma_prefetch_desc(&tm_Q);
       const uint64_t pol = l2_policy_evict_last();
       // cursors over this CTA's sequence of (unit, query tile): the next dO
-      // load, the next Q load, and the L2 prefetches kL2Ahead tiles ahead
+      // load and the next Q load
       struct Cursor {
         int u, i, hi, h;
       };
@@ -955,19 +941,9 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       auto advance = [&](Cursor& c) {
         if (++c.i >= c.hi) start(c, c.u + static_cast<int>(gridDim.x));
       };
-      Cursor cd, cq, pd, pq;
+      Cursor cd, cq;
       start(cd, blockIdx.x);
       start(cq, blockIdx.x);
-      start(pd, blockIdx.x);
-      start(pq, blockIdx.x);
-      for (int k = 0; k < kL2Ahead && pd.u < um.units; ++k) {
-        for (int b = 0; b < D / kBoxCols; ++b) {
-          tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, pd.i * kTile, pd.h);
-          tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, pq.i * kTile, pq.h);
-        }
-        advance(pd);
-        advance(pq);
-      }
       int next_do = 0, next_q = 0;  // loads issued (ring phases)
       uint64_t t_last = global_timer_ns();
       bool failed = false;
@@ -980,10 +956,6 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           for (int b = 0; b < D / kBoxCols; ++b)
             tma_load_3d(smem + Cfg::kOffdO + s * Cfg::kMD + b * kBoxBytes, &tm_dO, &bar[kKbDOFull0 + s],
                         b * kBoxCols, cd.i * kTile, cd.h, pol);
-          if (pd.u < um.units) {
-            for (int b = 0; b < D / kBoxCols; ++b) tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, pd.i * kTile, pd.h);
-            advance(pd);
-          }
           advance(cd);
           ++next_do;
           progressed = true;
@@ -995,10 +967,6 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
           for (int b = 0; b < D / kBoxCols; ++b)
             tma_load_3d(smem + Cfg::kOffQ + s * Cfg::kMD + b * kBoxBytes, &tm_Q, &bar[kKbQFull0 + s],
                         b * kBoxCols, cq.i * kTile, cq.h, pol);
-          if (pq.u < um.units) {
-            for (int b = 0; b < D / kBoxCols; ++b) tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, pq.i * kTile, pq.h);
-            advance(pq);
-          }
           advance(cq);
           ++next_q;
           progressed = true;

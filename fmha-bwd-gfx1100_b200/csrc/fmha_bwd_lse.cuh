@@ -534,11 +534,11 @@ __global__ void __launch_bounds__(DkvLseCfg<D>::kThreads, 1)
     }
   } else if (warp == 2) {
     // ---- TMA producer for the streamed Q_i and dO_i (two slots each; every
-    // key-tile CTA of the head reads them, so they are pulled into L2
-    // kL2Ahead query tiles ahead). Polls both "empty" barriers without
-    // blocking and issues whichever load can go.
+    // key-tile CTA of the head reads them, so they are L2 hits for all but
+    // the first). Polls both "empty" barriers without blocking and issues
+    // whichever load can go. No L2 prefetch ahead: it shares the TMA unit
+    // and L2 queues with the loads and cost 3 % of the call here.
     if (lane == 0) {
-      constexpr int kL2Ahead = 3;
       tma_prefetch_desc(&tm_dO);
       tma_prefetch_desc(&tm_Q);
       const uint64_t pol = l2_policy_evict_last();
@@ -546,11 +546,6 @@ __global__ void __launch_bounds__(DkvLseCfg<D>::kThreads, 1)
                            static_cast<int>(gridDim.x);
       const int total = my_items * mt;
       auto head_of = [&](int g) { return (static_cast<int>(blockIdx.x) + (g / mt) * static_cast<int>(gridDim.x)) / ntk; };
-      for (int i = 0; i < kL2Ahead && i < total; ++i)
-        for (int b = 0; b < D / kBoxCols; ++b) {
-          tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, (i % mt) * kTile, head_of(i));
-          tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, (i % mt) * kTile, head_of(i));
-        }
       int next_do = 0, next_q = 0;
       uint64_t t_last = global_timer_ns();
       bool failed = false;
@@ -564,10 +559,6 @@ __global__ void __launch_bounds__(DkvLseCfg<D>::kThreads, 1)
           for (int b = 0; b < D / kBoxCols; ++b)
             tma_load_3d(smem + Cfg::kOffQ + s * Cfg::kMD + b * kBoxBytes, &tm_Q, &bar[kLkQFull0 + s],
                         b * kBoxCols, i * kTile, hh, pol);
-          const int ahead = next_q + kL2Ahead;
-          if (ahead < total)
-            for (int b = 0; b < D / kBoxCols; ++b)
-              tma_prefetch_l2_3d(&tm_Q, b * kBoxCols, (ahead % mt) * kTile, head_of(ahead));
           ++next_q;
           progressed = true;
         }
@@ -579,10 +570,6 @@ __global__ void __launch_bounds__(DkvLseCfg<D>::kThreads, 1)
           for (int b = 0; b < D / kBoxCols; ++b)
             tma_load_3d(smem + Cfg::kOffdO + s * Cfg::kMD + b * kBoxBytes, &tm_dO, &bar[kLkDOFull0 + s],
                         b * kBoxCols, i * kTile, hh, pol);
-          const int ahead = next_do + kL2Ahead;
-          if (ahead < total)
-            for (int b = 0; b < D / kBoxCols; ++b)
-              tma_prefetch_l2_3d(&tm_dO, b * kBoxCols, (ahead % mt) * kTile, head_of(ahead));
           ++next_do;
           progressed = true;
         }

@@ -168,15 +168,6 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap,
       : "memory");
 }
 
-// Prefetch a 3-D tile into L2 only (no shared-memory destination).
-__device__ __forceinline__ void tma_prefetch_l2_3d(const void* tmap, int x, int y, int z) {
-  asm volatile(
-      "cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
-          reinterpret_cast<uint64_t>(tmap)),
-      "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-
 // L2 eviction-priority hints (createpolicy.fractional with fraction 1.0).
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
