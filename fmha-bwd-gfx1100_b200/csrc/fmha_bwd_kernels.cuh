@@ -748,13 +748,13 @@ __global__ void __launch_bounds__(DqCfg<D>::kThreads, 1)
 // query), dV [256,256+D), dK [256+D,256+2D) (lane = key, column = d).
 //
 // Warp roles: 0 TMA for V_j and the P stream; 1 MMA issuer for dP^T (and
-// TMEM owner) and, at D = 128, dV; 2 TMA for dO_i and Q_i; 3 MMA issuer for
-// dK at D = 128, for dV at D = 64; 4-11 dS warps (TMEM lane quarter =
-// warp % 4, query half = (warp - 4) / 4), which also write dK_j, dV_j; at
-// D = 64, warp 12 issues dK. At D = 64 each MMA group is short and a thread
-// between two of its groups spends a few hundred cycles on barrier waits and
-// commits even when nothing is outstanding, so three issuing threads keep
-// the pipe fed better.
+// TMEM owner); 2 TMA for dO_i and Q_i; 3 MMA issuer for dV; 4-11 dS warps
+// (TMEM lane quarter = warp % 4, query half = (warp - 4) / 4), which also
+// write dK_j, dV_j; 12 MMA issuer for dK. A thread between two of its MMA
+// groups spends a few hundred cycles on barrier waits and commits even when
+// nothing is outstanding, so three issuing threads keep the pipe fed better
+// (at D = 128 too: 4.9 % fewer SM cycles at FLUX than dV issued right behind
+// dP^T on one thread).
 template <int D>
 struct DkvCfg {
   static constexpr int kMD = (D / kBoxCols) * kBoxBytes;
@@ -773,12 +773,9 @@ struct DkvCfg {
   static constexpr int kSmemBytes = kTileBytes + kBarBytes + 1024;
   static constexpr int kDSWarps = 8;
   static constexpr int kFirstDSWarp = 4;
-  // D = 128: warp 1 issues dP^T and dV (both read dO_i, so its ring slot
-  // is released once both are done), warp 3 issues dK. D = 64: warps 1, 3
-  // and kDKWarp issue dP^T, dV and dK.
-  static constexpr bool kSplit = D == 64;
-  static constexpr int kDKWarp = kFirstDSWarp + kDSWarps;  // dK issuer (D = 64)
-  static constexpr int kThreads = 32 * (kDKWarp + (kSplit ? 1 : 0));
+  // warps 1, 3 and kDKWarp issue dP^T, dV and dK, one thread each
+  static constexpr int kDKWarp = kFirstDSWarp + kDSWarps;  // dK issuer
+  static constexpr int kThreads = 32 * (kDKWarp + 1);
   static constexpr uint32_t kTmemCols = 512;
   static constexpr int kNX = D == 128 ? 2 : 3;  // dP^T/dS^T buffers
   static constexpr uint32_t kColX = 0;          // + 128 * buffer
@@ -844,7 +841,7 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
     }
     for (int s = 0; s < SD; ++s) {
       mbar_init(&bar[kKbDOFull0 + s], 1);
-      mbar_init(&bar[kKbDOEmpty0 + s], Cfg::kSplit ? 2 : 1);
+      mbar_init(&bar[kKbDOEmpty0 + s], 2);  // dP^T and dV commits
     }
     for (int s = 0; s < SQ; ++s) {
       mbar_init(&bar[kKbQFull0 + s], 1);
@@ -989,12 +986,10 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
       }
     }
   } else if (warp == 1 || warp == 3 || warp == Cfg::kDKWarp) {
-    // ---- MMA issuers (the others keep the tensor pipe fed while one waits).
-    // Warp 1: dP^T_i into TMEM buffer i % NX, and at D = 128 dV_j += P^T
-    // dO_i right behind it (a dV issued after dK_(i-1), which waits for the
-    // dS warps, held dO_i's slot and with it dP^T_(i+2): 3.5 % more SM
-    // cycles at FLUX). D = 64: warp 3 issues dV. dK_j += dS^T Q_i: warp 3
-    // at D = 128, kDKWarp at D = 64.
+    // ---- MMA issuers, one thread per product (the others keep the tensor
+    // pipe fed while one waits). Warp 1: dP^T_i into TMEM buffer i % NX;
+    // warp 3: dV_j += P_ij^T dO_i; kDKWarp: dK_j += dS_ij^T Q_i. dO_i's
+    // ring slot is released by the dP^T and dV commits.
     if (lane == 0) {
       constexpr bool kB = Elem<T>::kBF16;
       constexpr uint32_t id_dP = make_idesc_f16<kB>(kTile, kTile, false, false);
@@ -1023,34 +1018,15 @@ __global__ void __launch_bounds__(DkvCfg<D>::kThreads, 1)
                         k > 0 ? 1u : 0u);
           }
           umma_commit(&bar[kKbXFull0 + x]);
-          if constexpr (!Cfg::kSplit) {
-            // dV_j += P_ij^T dO_i : A = P^T (MN-major, M = key), B = dO_i
-            // (MN-major, N = d); the accumulator must have been read out
-            const int sp = g % SP;
-            if (i == lo && tc > 0 && !mbar_wait(&bar[kKbAccEmpty], (tc - 1) & 1, ctx, 47)) { ok = false; break; }
-            if (!mbar_wait(&bar[kKbPFull0 + sp], (g / SP) & 1, ctx, 42)) { ok = false; break; }
-            tc_fence_after();
-            const uint64_t ddOm = make_sw128_desc(smem_u32(smem + Cfg::kOffdO + s * Cfg::kMD), kBoxBytes, 1024);
-            const uint64_t dP = make_sw128_desc(smem_u32(smem + Cfg::kOffP + sp * Cfg::kPT), kBoxBytes, 1024);
-#pragma unroll
-            for (int k = 0; k < kTile / 16; ++k) {
-              umma_f16_ss(tmem + Cfg::kColdV, desc_advance(dP, k * 2048), desc_advance(ddOm, k * 2048), id_dV,
-                          (i > lo || k > 0) ? 1u : 0u);
-            }
-            umma_commit(&bar[kKbPEmpty0 + sp]);
-          }
           umma_commit(&bar[kKbDOEmpty0 + s]);
         }
-        if (ok) {
-          umma_commit(&bar[kKbVEmpty]);             // V_j consumed
-          if (!Cfg::kSplit) umma_commit(&bar[kKbAcc]);  // dV complete
-        }
+        if (ok) umma_commit(&bar[kKbVEmpty]);  // V_j consumed
         }
         if (!ok) {
           umma_commit(&bar[kKbDrain]);
           mbar_wait_drain(&bar[kKbDrain], 0, timeout_ns);
         }
-      } else if (warp == 3 && Cfg::kSplit) {
+      } else if (warp == 3) {
         int g = 0, tc = 0;
         for (int u = blockIdx.x; u < um.units && ok; u += gridDim.x, ++tc) {
           int t, lo, hi, part;
