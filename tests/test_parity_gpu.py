@@ -344,3 +344,43 @@ def test_tail_items_split_into_parts(F, oracle_built, M, N, d, H, dtype):
     torch.cuda.synchronize()
     for nm, x, y in zip(("dQ", "dK", "dV"), a, c_):
         _assert_ok(O, nm, _f32(y), _f32(x), dtype)
+
+
+def _sweep_shapes():
+    """Seeded random shapes: ragged M and N, both head sizes and dtypes, head
+    counts that leave partly filled last waves (with and without split
+    parts), sized so the whole sweep runs in seconds."""
+    rng = np.random.default_rng(20261202)
+    shapes = []
+    for k in range(14):
+        d = 64 if k % 2 else 128
+        dtype = "fp16" if k % 3 == 0 else "bf16"
+        M = int(rng.integers(1, 2400))
+        N = int(rng.integers(1, 300)) * 8
+        H = int(rng.integers(1, 13))
+        shapes.append((M, N, d, H, dtype))
+    # shapes whose dK/dV or dQ tails are split into parts (items of 16+ steps)
+    shapes += [(2100, 264, 128, 9, "bf16"), (136, 2056, 64, 37, "fp16")]
+    return shapes
+
+
+@pytest.mark.parametrize("M,N,d,H,dtype", _sweep_shapes())
+def test_random_shape_sweep_per_head(F, oracle_built, M, N, d, H, dtype):
+    """Every head of every output within tolerance of the fp32 recompute
+    (per head, so a head written to the wrong place or a single ragged tile
+    cannot hide in a whole-tensor norm); outputs prefilled with NaN must be
+    fully written."""
+    O = oracle_built
+    Qb, Kb, Vb, Pb, dOb = O.make_inputs(M, N, d, H, dtype, seed=M * 7 + N + H)
+    dt = _dt(dtype)
+    ins = [_to_dev(x, dt) for x in (Qb, Kb, Vb, Pb, dOb)]
+    outs = [torch.full_like(ins[0], float("nan")), torch.full_like(ins[1], float("nan")),
+            torch.full_like(ins[2], float("nan"))]
+    got = F.fmha_bwd(*ins, out=outs)
+    torch.cuda.synchronize()
+    assert not any(torch.isnan(t).any().item() for t in got)
+    ref = _torch_reference(*ins)
+    for nm, g, r in zip(("dQ", "dK", "dV"), got, ref):
+        gf, rf = _f32(g), r.cpu().numpy()
+        for h in range(H):
+            _assert_ok(O, f"{nm}[{h}]", gf[h], rf[h], dtype)
